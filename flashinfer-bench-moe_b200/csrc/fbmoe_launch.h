@@ -1,0 +1,52 @@
+// fbmoe_launch.h -- internal host-side launchers shared by the C-ABI (moe_capi.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace fbmoe {
+
+// Offsets (bytes) of the sub-buffers inside the caller-provided workspace.
+struct Layout {
+  size_t status;       // uint32[4]  device status word(s)
+  size_t topk_idx;     // int32[T*8] global expert ids, canonical order
+  size_t topk_w;       // fp32[T*8]
+  size_t token_rows;   // int32[T*8] permuted row of each (token, slot), -1 if not local
+  size_t expert_cnt;   // int32[E_local]
+  size_t expert_poff;  // int32[E_local+1] padded row offsets
+  size_t n_blocks;     // int32[1]
+  size_t blocks;       // int4[max_blocks] (expert, row0, nrows, 0)
+  size_t row_token;    // int32[pcap]
+  size_t row_weight;   // fp32[pcap]
+  size_t inter;        // bf16[pcap * 2048]  SwiGLU output, expert-contiguous rows
+  size_t pair_out;     // bf16[pcap * 7168]  weighted per-(token, expert) rows
+  size_t total;        // bytes
+  int pcap;            // row capacity (multiple of 128)
+  int max_blocks;
+};
+
+Layout make_layout(int T, int E_local);
+
+// Router: topk_idx/topk_w for T tokens; zeroes status[0].
+cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, float scale, int32_t* topk_idx,
+                         float* topk_w, uint32_t* status, cudaStream_t stream);
+
+// Histogram / padded offsets / deterministic permutation / GEMM block list.
+cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
+                           int bn, const Layout& L, uint8_t* ws, cudaStream_t stream);
+
+// GEMM1 + SwiGLU: inter[row, :] for every local (token, expert) row.
+cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const uint8_t* hidden, const float* hidden_scale, int T,
+                         const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
+                         cudaStream_t stream);
+
+// GEMM2 (W2 dequantised to bf16 on chip) x routing weight -> pair_out rows.
+cudaError_t launch_gemm2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, const float* w2_scale,
+                         int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream);
+
+// out[t, :] = sum of the token's pair rows, fp32 accumulation, bf16 result.
+cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out_bf16, cudaStream_t stream);
+
+}  // namespace fbmoe

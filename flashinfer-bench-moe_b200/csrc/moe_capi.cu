@@ -1,0 +1,215 @@
+// moe_capi.cu -- the C ABI (include/fbmoe.h): argument checks, workspace
+// layout, TMA descriptors and the launch chain of the fused MoE forward.
+//
+// Launch chain of fbmoe_forward (reference fused_moe, solution/triton/main.py:
+// 2668-2774, five stages):
+//   route -> permute (histogram / padded scan / deterministic scatter)
+//         -> GEMM1 + SwiGLU (tcgen05) -> GEMM2 x weight (tcgen05) -> combine.
+// Nothing synchronises the host and nothing allocates device memory; the caller
+// owns the workspace (the reference keeps a module-global 15000-token one).
+#include <cudaTypedefs.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/fbmoe.h"
+#include "fbmoe_common.cuh"
+#include "fbmoe_launch.h"
+
+namespace fbmoe {
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+Layout make_layout(int T, int E_local) {
+  Layout L;
+  const size_t tt = (size_t)(T > 0 ? T : 0);
+  const int el = E_local > 0 ? E_local : 0;
+  long pcap = (long)tt * kTopK + (long)kRowAlign * el;
+  pcap = (long)align_up((size_t)pcap, 128);
+  if (pcap < 128) pcap = 128;
+  L.pcap = (int)pcap;
+  L.max_blocks = (int)(pcap / kRowAlign);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  L.status = take(16);
+  L.topk_idx = take(tt * kTopK * 4);
+  L.topk_w = take(tt * kTopK * 4);
+  L.token_rows = take(tt * kTopK * 4);
+  L.expert_cnt = take((size_t)el * 4);
+  L.expert_poff = take((size_t)(el + 1) * 4);
+  L.n_blocks = take(16);
+  L.blocks = take((size_t)L.max_blocks * 16);
+  L.row_token = take((size_t)pcap * 4);
+  L.row_weight = take((size_t)pcap * 4);
+  L.inter = take((size_t)pcap * kInter * 2);
+  L.pair_out = take((size_t)pcap * kHidden * 2);
+  L.total = off;
+  return L;
+}
+
+static int choose_block_rows(int T, int E_local) {
+  (void)E_local;
+  if (T <= 256) return 16;
+  if (T <= 1024) return 32;
+  if (T <= 4096) return 64;
+  return 128;
+}
+
+// ---------------------------------------------------------------- driver ----
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+static bool get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+// 2-D K-major tile map with 128-byte swizzle.  inner = K extent (elements).
+static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
+                     uint64_t rows, uint32_t box_inner, uint32_t box_rows) {
+  if (!get_encode()) return FBMOE_ERR_DRIVER;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FBMOE_OK : FBMOE_ERR_DRIVER;
+}
+
+static int num_sms_of_current_device() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 64 && cache[dev]) return cache[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+static int from_cuda(cudaError_t e) { return e == cudaSuccess ? FBMOE_OK : (int)e; }
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace fbmoe
+
+using namespace fbmoe;
+
+extern "C" {
+
+size_t fbmoe_workspace_size(int T, int E_local) {
+  if (T < 0 || E_local < 1 || E_local > kExperts) return 0;
+  return make_layout(T, E_local).total;
+}
+
+int fbmoe_block_rows(int T, int E_local) { return choose_block_rows(T, E_local); }
+
+int fbmoe_workspace_layout(int T, int E_local, int64_t* offsets) {
+  if (offsets == nullptr) return FBMOE_ERR_NULL_POINTER;
+  if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
+  const Layout L = make_layout(T, E_local);
+  const int64_t v[FBMOE_LAYOUT_FIELDS] = {
+      (int64_t)L.status,   (int64_t)L.topk_idx,  (int64_t)L.topk_w,     (int64_t)L.token_rows, (int64_t)L.expert_cnt,
+      (int64_t)L.expert_poff, (int64_t)L.n_blocks, (int64_t)L.blocks,   (int64_t)L.row_token,  (int64_t)L.row_weight,
+      (int64_t)L.inter,    (int64_t)L.pair_out,  (int64_t)L.total,      (int64_t)L.pcap};
+  memcpy(offsets, v, sizeof v);
+  return FBMOE_OK;
+}
+
+int fbmoe_route(const float* routing_logits, const void* routing_bias, int T, float routed_scaling_factor,
+                int32_t* topk_idx, float* topk_weights, void* stream) {
+  if (T < 0) return FBMOE_ERR_INVALID_ARG;
+  if (T == 0) return FBMOE_OK;
+  if (!routing_logits || !routing_bias || !topk_idx || !topk_weights) return FBMOE_ERR_NULL_POINTER;
+  if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16)) return FBMOE_ERR_MISALIGNED;
+  return from_cuda(launch_route(routing_logits, routing_bias, T, routed_scaling_factor, topk_idx, topk_weights,
+                                nullptr, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int fbmoe_forward(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                  int local_expert_offset, float routed_scaling_factor, void* out, void* workspace,
+                  size_t workspace_bytes, void* stream_) {
+  if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
+  if (T == 0) return FBMOE_OK;
+  if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale || !gemm1_weights ||
+      !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !out || !workspace)
+    return FBMOE_ERR_NULL_POINTER;
+  if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
+      !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(out, 16) || !aligned(workspace, 256))
+    return FBMOE_ERR_MISALIGNED;
+  const Layout L = make_layout(T, E_local);
+  if (workspace_bytes < L.total) return FBMOE_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const int bn = choose_block_rows(T, E_local);
+  const int sms = num_sms_of_current_device();
+
+  CUtensorMap tm_w1, tm_w2, tm_inter;
+  int rc = encode_2d(&tm_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm1_weights, kHidden, (uint64_t)E_local * kGemm1N,
+                     128, 64);
+  if (rc) return rc;
+  rc = encode_2d(&tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 128,
+                 128);
+  if (rc) return rc;
+  rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
+                 (uint32_t)bn);
+  if (rc) return rc;
+
+  int32_t* topk_idx = reinterpret_cast<int32_t*>(ws + L.topk_idx);
+  float* topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+  cudaError_t e = launch_route(routing_logits, routing_bias, T, routed_scaling_factor, topk_idx, topk_w,
+                               reinterpret_cast<uint32_t*>(ws + L.status), stream);
+  if (e != cudaSuccess) return from_cuda(e);
+  e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, L, ws, stream);
+  if (e != cudaSuccess) return from_cuda(e);
+  e = launch_gemm1(&tm_w1, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
+                   gemm1_weights_scale, E_local, bn, L, ws, sms, stream);
+  if (e != cudaSuccess) return from_cuda(e);
+  e = launch_gemm2(&tm_w2, &tm_inter, gemm2_weights_scale, E_local, bn, L, ws, sms, stream);
+  if (e != cudaSuccess) return from_cuda(e);
+  e = launch_reduce(T, L, ws, out, stream);
+  return from_cuda(e);
+}
+
+int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream_) {
+  if (!workspace || !status) return FBMOE_ERR_NULL_POINTER;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  cudaError_t e = cudaMemcpyAsync(status, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return from_cuda(e);
+  return *status ? FBMOE_ERR_DEVICE_STATUS : FBMOE_OK;
+}
+
+const char* fbmoe_error_string(int code) {
+  switch (code) {
+    case FBMOE_OK: return "ok";
+    case FBMOE_ERR_INVALID_ARG: return "invalid argument (T < 0 or E_local outside 1..256)";
+    case FBMOE_ERR_WORKSPACE_TOO_SMALL: return "workspace smaller than fbmoe_workspace_size(T, E_local)";
+    case FBMOE_ERR_NULL_POINTER: return "null pointer argument";
+    case FBMOE_ERR_MISALIGNED: return "misaligned pointer (tensors need 16-byte, workspace 256-byte alignment)";
+    case FBMOE_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected a tensor map";
+    case FBMOE_ERR_DEVICE_STATUS: return "a kernel reported a device-side error (bounded wait expired)";
+    default: break;
+  }
+  if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
+  return "unknown fbmoe error";
+}
+
+int fbmoe_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,183 @@
+// moe_permute.cu -- per-expert histogram, padded prefix sum and deterministic
+// token permutation into expert-contiguous rows, plus the GEMM block list.
+//
+// Counterpart of the reference's count / scan / permute kernels
+// (solution/triton/main.py:1063-1238) with two differences:
+//  * the order of rows inside an expert is token-ascending (deterministic; the
+//    reference uses an atomic cursor, main.py:1150-1160);
+//  * each expert's row segment starts at a multiple of 16 rows, so every GEMM
+//    block of BN rows starts aligned, and the number of local experts is a
+//    runtime value (32, 64, 128 or 256 for expert-parallel shards).
+// The activations are NOT copied (reference main.py:1241-1271): GEMM1 gathers
+// token rows directly.
+//
+// One CTA of 1024 threads; tokens are processed in chunks of 1024.  Within a
+// chunk, a token's rank inside an expert is the number of set bits before it
+// in that expert's 1024-bit membership mask, which is order-independent.
+#include "fbmoe_common.cuh"
+#include "fbmoe_launch.h"
+
+namespace fbmoe {
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kWordsPerChunk = kThreads / 32;
+constexpr int kMaxLocal = 256;
+
+struct PermuteSmem {
+  int count[kMaxLocal];
+  int poff[kMaxLocal + 1];
+  int bstart[kMaxLocal + 1];
+  int cursor[kMaxLocal];
+  int chunk_total[kMaxLocal];
+  uint32_t bits[kMaxLocal][kWordsPerChunk];
+  uint16_t wpre[kMaxLocal][kWordsPerChunk];
+  int scan_tmp[2][kMaxLocal / 32];
+};
+
+// Exclusive scan of one value per thread over threads 0..255 (8 warps).
+__device__ __forceinline__ int block_excl_scan_256(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) tmp[warp] = x;
+  named_barrier_sync(1, 256);
+  int base = 0, all = 0;
+#pragma unroll
+  for (int w = 0; w < kMaxLocal / 32; ++w) {
+    const int tw = tmp[w];
+    base += (w < warp) ? tw : 0;
+    all += tw;
+  }
+  *total = all;
+  return base + x - v;
+}
+
+__global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __restrict__ topk_idx,
+                                                          const float* __restrict__ topk_w, int T, int E_local,
+                                                          int local_offset, int bn, int32_t* __restrict__ expert_cnt,
+                                                          int32_t* __restrict__ expert_poff,
+                                                          int32_t* __restrict__ n_blocks, int4* __restrict__ blocks,
+                                                          int max_blocks, int32_t* __restrict__ row_token,
+                                                          float* __restrict__ row_weight,
+                                                          int32_t* __restrict__ token_rows,
+                                                          uint32_t* __restrict__ status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  PermuteSmem& S = *reinterpret_cast<PermuteSmem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+
+  for (int e = tid; e < kMaxLocal; e += kThreads) S.count[e] = 0;
+  __syncthreads();
+
+  // Phase A: counts.
+  for (int t = tid; t < T; t += kThreads) {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int e = topk_idx[(size_t)t * kTopK + k] - local_offset;
+      if ((unsigned)e < (unsigned)E_local) atomicAdd(&S.count[e], 1);
+    }
+  }
+  __syncthreads();
+
+  // Phase B: padded offsets and the GEMM block list (threads 0..255 = experts).
+  if (tid < kMaxLocal) {
+    const int e = tid;
+    const int c = (e < E_local) ? S.count[e] : 0;
+    const int padded = (c + kRowAlign - 1) / kRowAlign * kRowAlign;
+    const int nb = (c + bn - 1) / bn;
+    int tot_rows, tot_blocks;
+    const int off = block_excl_scan_256(padded, S.scan_tmp[0], &tot_rows);
+    const int boff = block_excl_scan_256(nb, S.scan_tmp[1], &tot_blocks);
+    if (e < E_local) {
+      S.poff[e] = off;
+      S.cursor[e] = off;
+      expert_cnt[e] = c;
+      expert_poff[e] = off;
+      for (int j = 0; j < nb; ++j) {
+        const int b = boff + j;
+        if (b < max_blocks) blocks[b] = make_int4(e, off + j * bn, min(bn, c - j * bn), 0);
+      }
+    }
+    if (e == 0) {
+      expert_poff[E_local] = tot_rows;
+      *n_blocks = min(tot_blocks, max_blocks);
+      if (tot_blocks > max_blocks) atomicOr(status, kStatusBadTile);
+    }
+  }
+  __syncthreads();
+
+  // Phase C: deterministic scatter, chunk by chunk.
+  for (int base = 0; base < T; base += kThreads) {
+    for (int i = tid; i < kMaxLocal * kWordsPerChunk; i += kThreads) (&S.bits[0][0])[i] = 0u;
+    __syncthreads();
+    const int t = base + tid;
+    int le[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      le[k] = -1;
+      if (t < T) {
+        const int e = topk_idx[(size_t)t * kTopK + k] - local_offset;
+        if ((unsigned)e < (unsigned)E_local) {
+          le[k] = e;
+          atomicOr(&S.bits[e][warp], 1u << lane);
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < E_local) {
+      int run = 0;
+      for (int w = 0; w < kWordsPerChunk; ++w) {
+        S.wpre[tid][w] = (uint16_t)run;
+        run += __popc(S.bits[tid][w]);
+      }
+      S.chunk_total[tid] = run;
+    }
+    __syncthreads();
+    if (t < T) {
+      const uint32_t below = (1u << lane) - 1u;
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        const int e = le[k];
+        int row = -1;
+        if (e >= 0) {
+          row = S.cursor[e] + S.wpre[e][warp] + __popc(S.bits[e][warp] & below);
+          row_token[row] = t;
+          row_weight[row] = topk_w[(size_t)t * kTopK + k];
+        }
+        token_rows[(size_t)t * kTopK + k] = row;
+      }
+    }
+    __syncthreads();
+    if (tid < E_local) S.cursor[tid] += S.chunk_total[tid];
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
+                           int bn, const Layout& L, uint8_t* ws, cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int smem = (int)sizeof(PermuteSmem);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return err;
+    attr_set[dev] = true;
+  }
+  permute_kernel<<<1, kThreads, smem, stream>>>(
+      topk_idx, topk_w, T, E_local, local_offset, bn, reinterpret_cast<int32_t*>(ws + L.expert_cnt),
+      reinterpret_cast<int32_t*>(ws + L.expert_poff), reinterpret_cast<int32_t*>(ws + L.n_blocks),
+      reinterpret_cast<int4*>(ws + L.blocks), L.max_blocks, reinterpret_cast<int32_t*>(ws + L.row_token),
+      reinterpret_cast<float*>(ws + L.row_weight), reinterpret_cast<int32_t*>(ws + L.token_rows),
+      reinterpret_cast<uint32_t*>(ws + L.status));
+  return cudaGetLastError();
+}
+
+}  // namespace fbmoe

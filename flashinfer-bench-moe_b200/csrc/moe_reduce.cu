@@ -1,0 +1,60 @@
+// moe_reduce.cu -- per-token combine of the weighted (token, expert) rows.
+//
+// Reference counterpart: reduce_add_kernel_small/large (solution/triton/main.py:
+// 1604-1714), which adds the pair rows with bf16 __hadd2.  Here the sum runs in
+// fp32 over the token's slots in fixed slot order (deterministic) and is rounded
+// to bf16 once.  Tokens with no local expert get a zero row, as in the reference.
+#include "fbmoe_common.cuh"
+#include "fbmoe_launch.h"
+
+namespace fbmoe {
+namespace {
+
+constexpr int kReduceThreads = 128;               // 128 threads x 8 bf16 = 1024 columns
+constexpr int kReduceChunks = kHidden / (kReduceThreads * 8);  // 7
+
+__global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __nv_bfloat16* __restrict__ pair_out,
+                                                                const int32_t* __restrict__ token_rows,
+                                                                __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.y;
+  const int col = (blockIdx.x * kReduceThreads + threadIdx.x) * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  const int4* rows4 = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
+  const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
+  const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    if (rows[k] >= 0) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(pair_out + (size_t)rows[k] * kHidden + col));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] += __uint_as_float(w[i] << 16);
+        acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    }
+  }
+  uint4 o;
+  uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    ow[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * kHidden + col) = o;
+}
+
+}  // namespace
+
+cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out_bf16, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  dim3 grid(kReduceChunks, T);
+  reduce_kernel<<<grid, kReduceThreads, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(ws + L.pair_out),
+                                                     reinterpret_cast<const int32_t*>(ws + L.token_rows),
+                                                     reinterpret_cast<__nv_bfloat16*>(out_bf16));
+  return cudaGetLastError();
+}
+
+}  // namespace fbmoe

@@ -1,0 +1,105 @@
+/*
+ * fbmoe.h -- C ABI of the B200-native fused FP8 block-scale DeepSeek-V3 MoE
+ * operator (libfbmoe.so).  Plain pointers, sizes and a CUDA stream handle; no
+ * framework types.  All tensor pointers are device pointers to contiguous
+ * row-major data on the current CUDA device; every call is asynchronous on
+ * `stream` and performs no host synchronisation and no device allocation.
+ *
+ * These entry points replace the launch chain of the reference operator
+ * weichengz0616/flashinfer-bench-moe, solution/triton/main.py:
+ *   fused_moe()                        main.py:2668-2774  -> fbmoe_forward
+ *   fusedRoutePermuteCopyIntoWrapper   main.py:2177-2326  -> fbmoe_route (+ permute inside fbmoe_forward)
+ *   gemm1_aot + actQuantWrapper        main.py:367-421, 1572-1602, 2720-2737
+ *   gemm2_aot + reduceAddWrapper       main.py:748-806, 1686-1714, 2752-2771
+ *   FusedMoeWorkspace                  main.py:2628-2665  -> fbmoe_workspace_size / caller-owned workspace
+ *
+ * Return codes: 0 on success; FBMOE_ERR_* (negative) for invalid arguments;
+ * a positive value is a cudaError_t from a launch.  fbmoe_error_string()
+ * describes any code.
+ */
+#ifndef FBMOE_H_
+#define FBMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FBMOE_API __attribute__((visibility("default")))
+#else
+#define FBMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FBMOE_HIDDEN 7168
+#define FBMOE_INTERMEDIATE 2048
+#define FBMOE_NUM_EXPERTS 256
+#define FBMOE_TOP_K 8
+
+#define FBMOE_OK 0
+#define FBMOE_ERR_INVALID_ARG (-1)
+#define FBMOE_ERR_WORKSPACE_TOO_SMALL (-2)
+#define FBMOE_ERR_NULL_POINTER (-3)
+#define FBMOE_ERR_MISALIGNED (-4)
+#define FBMOE_ERR_DRIVER (-5)
+#define FBMOE_ERR_DEVICE_STATUS (-6)
+
+/* Bytes of device workspace fbmoe_forward needs for T tokens and E_local local
+ * experts (the reference sizes one global workspace for 15000 tokens,
+ * main.py:2657; here the caller owns it and sizes it per call). */
+FBMOE_API size_t fbmoe_workspace_size(int T, int E_local);
+
+/* The fused MoE forward (reference fused_moe, main.py:2668-2774).
+ *   routing_logits      fp32 [T, 256]
+ *   routing_bias        bf16 [256]
+ *   hidden_states       float8_e4m3fn [T, 7168]
+ *   hidden_states_scale fp32 [56, T]            (1x128 block scales, transposed)
+ *   gemm1_weights       float8_e4m3fn [E_local, 4096, 7168]
+ *   gemm1_weights_scale fp32 [E_local, 32, 56]  (128x128 block scales)
+ *   gemm2_weights       float8_e4m3fn [E_local, 7168, 2048]
+ *   gemm2_weights_scale fp32 [E_local, 56, 16]
+ *   out                 bf16 [T, 7168]          (written, not accumulated)
+ * local_expert_offset: first global expert owned by this call (0..255);
+ * E_local in {1..256}; workspace: >= fbmoe_workspace_size(T, E_local) bytes,
+ * 256-byte aligned.  The result for a token is the sum over its selected
+ * experts that are local. */
+FBMOE_API int fbmoe_forward(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                  int local_expert_offset, float routed_scaling_factor, void* out, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* DeepSeek-V3 no-aux routing only (reference main.py:2522-2553 / fusedGatingKernel
+ * main.py:851-1038).  topk_idx int32 [T, 8] global expert ids in canonical order
+ * (descending s+bias, ascending id among equals); topk_weights fp32 [T, 8]. */
+FBMOE_API int fbmoe_route(const float* routing_logits, const void* routing_bias, int T, float routed_scaling_factor,
+                int32_t* topk_idx, float* topk_weights, void* stream);
+
+/* Byte offsets of the forward's intermediate buffers inside the workspace, for
+ * inspection by tests.  `offsets` receives FBMOE_LAYOUT_FIELDS values in this
+ * order: status, topk_idx, topk_w, token_rows, expert_cnt, expert_poff,
+ * n_blocks, blocks, row_token, row_weight, inter, pair_out, total, row_capacity. */
+#define FBMOE_LAYOUT_FIELDS 14
+FBMOE_API int fbmoe_workspace_layout(int T, int E_local, int64_t* offsets);
+
+/* Block rows (GEMM N tile) the forward picks for T tokens and E_local experts. */
+FBMOE_API int fbmoe_block_rows(int T, int E_local);
+
+/* Reads the device status word of the last forward on this workspace
+ * (synchronises `stream`).  0 = clean; non-zero = a bounded wait expired inside
+ * a kernel (bit 0 producer, 1 MMA, 2 epilogue, 3 converter, 5 drain) or the
+ * block list overflowed (bit 4). */
+FBMOE_API int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream);
+
+FBMOE_API const char* fbmoe_error_string(int code);
+
+/* Library version (major*10000 + minor*100 + patch). */
+FBMOE_API int fbmoe_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FBMOE_H_ */
