@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the fused FP8 block-scale DeepSeek-V3 MoE (main.py::fused_moe) on B200.
+
+Workload (one "step" = one MoE layer call): BASELINE config 3 -- T = 8192 tokens,
+all 256 experts, expert parallelism over N = --gpus ranks (E_local = 256/N,
+local_expert_offset = rank * E_local).  Hidden states and routing logits are
+replicated on every rank; each rank computes its experts' un-rounded fp32 partial
+and NCCL reduce-scatter sums the partials (rank r keeps tokens
+[r*T/N, (r+1)*T/N)).  At N = 1 the step is the plain fused_moe call.
+
+value  = tokens/s of the whole job (T * steps / max-over-ranks device time).
+e2e    = the same through the public API with the activations copied from pinned
+         host memory and the rank's output rows copied back, inside the timing.
+On N = 1 the line also carries the decode sweep (config 1: T = 1..64, 32 local
+experts, HBM roofline) and prefill points (config 2: skewed routing, FP8 tensor
+roofline), each measured with L2 flushed between calls.
+
+`--impl reference` times the reference operator's own CPU algorithm (the oracle
+restatement of run(), solution/triton/main.py:2430-2609) on a bounded sample of
+the same workload on the host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "flashinfer-bench-moe_b200")
+sys.path.insert(0, PKG)
+
+T_EP = 8192
+E_TOTAL = 256
+H = 7168
+BYTES_PER_EXPERT = 29_360_128 + 14_680_064 + 7_168 + 3_584  # W1 + W2 fp8 + their fp32 scales
+BYTES_PER_TOKEN = 7_168 + 224 + 1_024 + 14_336             # hidden fp8 + scales + logits + bf16 out
+FLOPS_PER_PAIR = 2 * (4096 * 7168 + 7168 * 2048)
+GEMM1_FLOPS_PER_PAIR = 2 * 4096 * 7168
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.dev = device_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 6]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[0]) for r in rows if r[0].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][1]) if rows[0][1].strip().replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- our arm
+def ep_inputs(world, rank):
+    import fbmoe_workloads as W
+    E_local = E_TOTAL // world
+    off = rank * E_local
+    weights = W.make_weights(E_local, 1000 + rank, "cuda")
+    inp = W.make_inputs(T_EP, seed=0, config="standard", device="cuda", E_local=E_local,
+                        local_expert_offset=off, weights=weights)
+    return inp, E_local, off
+
+
+def make_step(inp, world, rank):
+    import fbmoe_lib as L
+    args = [inp[k] for k in ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale",
+                             "gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+    off, scale = inp["local_expert_offset"], inp["routed_scaling_factor"]
+    T = T_EP
+    if world == 1:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            L.forward(*args, off, scale, out=out, check=False)
+            return out
+        return step, out
+    import torch.distributed as dist
+    partial = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    shard = torch.empty((T // world, H), dtype=torch.float32, device="cuda")
+    out = torch.empty((T // world, H), dtype=torch.bfloat16, device="cuda")
+
+    def step():
+        L.forward(*args, off, scale, out=partial, check=False, partial_f32=True)
+        dist.reduce_scatter_tensor(shard, partial)
+        out.copy_(shard)
+        return out
+    return step, out
+
+
+def local_pairs(inp, E_local, off):
+    import fbmoe_lib as L
+    idx, _ = L.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
+    loc = (idx >= off) & (idx < off + E_local)
+    return int(loc.sum().item()), int(torch.unique(idx[loc]).numel())
+
+
+def run_ours(args, world, rank, local):
+    import fbmoe_lib as L
+    peaks = load_peaks()
+    inp, E_local, off = ep_inputs(world, rank)
+    step, out = make_step(inp, world, rank)
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.profile_begin(args.steps)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        barrier(world)
+    stage_ms, nfwd = L.profile_end()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    ms_per_step = ms / args.steps
+    value = T_EP * args.steps / (ms / 1e3)
+
+    # roofline of the dominant kernel (per launch, averaged over the timed region, this rank)
+    pairs, active = local_pairs(inp, E_local, off)
+    per_stage = {n: stage_ms[i] / max(nfwd, 1) for i, n in enumerate(L.STAGES)}
+    dom = max(("gemm1", "gemm2"), key=lambda n: per_stage[n])
+    if dom == "gemm1":
+        flops = pairs * GEMM1_FLOPS_PER_PAIR
+        peak = 2.0 * peaks["bf16_tflops_sustained"]
+        peak_note = "fp8 dense = 2x the measured sustained bf16 cuBLAS figure"
+    else:
+        flops = pairs * 2 * 7168 * 2048
+        peak = peaks["bf16_tflops_sustained"]
+        peak_note = "f16 dense = the measured sustained bf16 cuBLAS figure"
+    achieved = flops / (per_stage[dom] / 1e3) / 1e12
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(f"{dom}_ep{world}_bytes_per_launch")
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} ({peak_note})", "algorithmic_flops_per_launch": flops,
+                "stage_ms_per_step": {k: round(v, 4) for k, v in per_stage.items()}, "local_pairs": pairs,
+                "active_local_experts": active}
+
+    e2e = run_e2e(args, world, rank, inp, E_local, off)
+    line = {
+        "metric": "tokens/s per MoE layer call (DS-V3 FP8 MoE, T=8192, 256 experts, EP over N GPUs)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8_e4m3 GEMM1 / f16 GEMM2, fp32 accumulate",
+        "data": "synthetic (seeded N(0,1) activations/logits, N(0,0.02) weights, FP8 block-quantised)",
+        "config": {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
+                   "parallelism": f"ep{world}", "combine": "none" if world == 1 else "nccl reduce_scatter fp32",
+                   "l2": "inputs larger than L2 (weights %.1f GB per GPU)" % (E_local * BYTES_PER_EXPERT / 1e9)},
+        "roofline": roofline, "e2e": e2e, "gpu_launches": 5 * args.steps, "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_sweep:
+        line["decode_sweep"] = decode_sweep(peaks)
+        line["prefill"] = prefill_points(peaks)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline_ep(inp, E_local, budget_s=args.cpu_budget)
+    return line
+
+
+def run_e2e(args, world, rank, inp, E_local, off):
+    """Public API with host buffers: H2D activations, fused_moe (+ combine), D2H of this rank's rows."""
+    import fbmoe_lib as L
+    names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    host = {k: inp[k].cpu().pin_memory() for k in names}
+    dev = {k: torch.empty_like(inp[k]) for k in names}
+    w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+    rows = T_EP // world
+    out_host = torch.empty((rows, H), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+    if world > 1:
+        import torch.distributed as dist
+        partial = torch.empty((T_EP, H), dtype=torch.float32, device="cuda")
+        shard = torch.empty((rows, H), dtype=torch.float32, device="cuda")
+
+    def one():
+        for k in names:
+            dev[k].copy_(host[k], non_blocking=True)
+        if world == 1:
+            o = L.forward(dev["routing_logits"], dev["routing_bias"], dev["hidden_states"],
+                          dev["hidden_states_scale"], *w, off, inp["routed_scaling_factor"])
+        else:
+            L.forward(dev["routing_logits"], dev["routing_bias"], dev["hidden_states"], dev["hidden_states_scale"],
+                      *w, off, inp["routed_scaling_factor"], out=partial, partial_f32=True)
+            dist.reduce_scatter_tensor(shard, partial)
+            o = shard.to(torch.bfloat16)
+        out_host.copy_(o, non_blocking=True)
+
+    n = max(3, min(args.steps, 10))
+    for _ in range(2):
+        one()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        one()
+    e.record()
+    barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e), world)
+    return {"value": round(T_EP * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms / n, 4)}
+
+
+def flush_l2(buf):
+    buf.add_(1)  # 256 MB read+write > 126 MB L2
+
+
+def time_calls(fn, iters, flush):
+    ts = []
+    for _ in range(3):
+        fn()
+    for _ in range(iters):
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    return statistics.median(ts)
+
+
+def decode_sweep(peaks):
+    import fbmoe_lib as L
+    import fbmoe_workloads as W
+    weights = W.make_weights(32, 4242, "cuda")
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    res = []
+    for T in (1, 2, 4, 8, 16, 32, 64):
+        inp = W.make_inputs(T, seed=T, config="standard", device="cuda", weights=weights)
+        args = W.as_args(inp)
+        us = 1e3 * time_calls(lambda: L.forward(*args, check=False), 30, lambda: flush_l2(buf))
+        pairs, active = local_pairs(inp, 32, 0)
+        nbytes = active * BYTES_PER_EXPERT + BYTES_PER_TOKEN * T + 512
+        gbs = nbytes / (us / 1e6) / 1e9
+        res.append({"T": T, "us_per_call": round(us, 2), "active_experts": active, "local_pairs": pairs,
+                    "algorithmic_bytes": nbytes, "hbm_gbs": round(gbs, 1),
+                    "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)})
+    del weights
+    return {"config": "config1 decode, 32 local experts, offset 0, L2 flushed between calls",
+            "peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"], "points": res}
+
+
+def prefill_points(peaks):
+    import fbmoe_lib as L
+    import fbmoe_workloads as W
+    weights = W.make_weights(32, 4242, "cuda")
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    res = []
+    for T in (1024, 4096, 8192):
+        inp = W.make_inputs(T, seed=T, config="skew", device="cuda", weights=weights)
+        args = W.as_args(inp)
+        ms = time_calls(lambda: L.forward(*args, check=False), 10, lambda: flush_l2(buf))
+        pairs, active = local_pairs(inp, 32, 0)
+        flops = pairs * FLOPS_PER_PAIR
+        tf = flops / (ms / 1e3) / 1e12
+        # mixed precision: GEMM1 (2/3 of FLOPs) at fp8 rate, GEMM2 at f16 rate
+        peak_mixed = 1.0 / ((2 / 3) / (2 * peaks["bf16_tflops"]) + (1 / 3) / peaks["bf16_tflops"])
+        res.append({"T": T, "us_per_call": round(ms * 1e3, 1), "local_pairs": pairs, "tflops": round(tf, 1),
+                    "frac_tensor_mixed_peak": round(tf / peak_mixed, 4),
+                    "frac_fp8_peak": round(tf / (2 * peaks["bf16_tflops"]), 4)})
+    return {"config": "config2 prefill, +3.0 bias on 4 local experts, 32 local experts",
+            "peak_note": "fp8 peak = 2x measured bf16 burst; mixed peak weights GEMM1 fp8 and GEMM2 f16 by FLOPs",
+            "points": res}
+
+
+# --------------------------------------------------------------------------- CPU baselines
+def cpu_baseline_ep(inp, E_local, budget_s=20.0, n_exp=4):
+    cores = torch.get_num_threads()
+    keys = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    cpu = {k: inp[k].cpu() for k in keys}
+    cpu["local_expert_offset"] = inp["local_expert_offset"]
+    cpu["routed_scaling_factor"] = inp["routed_scaling_factor"]
+    est, spent, samples = [], 0.0, 0
+    e0 = 0
+    while spent < budget_s and samples < 8:
+        for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale"):
+            cpu[k] = inp[k][e0:e0 + n_exp].cpu()
+        full, used = _sample_block(cpu, inp, e0, n_exp, E_local)
+        est.append(full)
+        spent += used
+        samples += 1
+        e0 = (e0 + 37 * n_exp) % (E_local - n_exp + 1)
+    call_s = statistics.mean(est)
+    return {"value": round(T_EP / call_s, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{samples} samples of {n_exp} of {E_local} experts with all their routed tokens of T={T_EP}, "
+                      f"oracle (torch fp32 CPU + C router) extrapolated x{E_local // n_exp}; "
+                      f"{spent:.1f} s of CPU work",
+            "seconds_per_call_estimate": round(call_s, 2)}
+
+
+def _sample_block(cpu, inp, e0, n_exp, E_local):
+    """Oracle on experts [e0, e0+n_exp) of the shard (all their routed tokens): returns
+    (extrapolated seconds for the whole shard, seconds actually spent)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    t0 = time.perf_counter()
+    routing = O.route(cpu["routing_logits"], cpu["routing_bias"], cpu["routed_scaling_factor"])
+    t_route = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    O.run(cpu["routing_logits"], cpu["routing_bias"], cpu["hidden_states"], cpu["hidden_states_scale"],
+          cpu["gemm1_weights"], cpu["gemm1_weights_scale"], cpu["gemm2_weights"], cpu["gemm2_weights_scale"],
+          int(inp["local_expert_offset"]) + e0, cpu["routed_scaling_factor"], routing=routing)
+    t_exp = time.perf_counter() - t1
+    return t_route + t_exp * (E_local / n_exp), t_route + t_exp
+
+
+def run_reference(args, world, rank):
+    """The reference algorithm on the host cores (oracle restatement of run()), rank 0 only."""
+    if rank != 0:
+        return None
+    import fbmoe_workloads as W
+    torch.set_num_threads(os.cpu_count() or 1)
+    E_local = E_TOTAL // world
+    n_exp = 2
+    logits, bias, hs, hs_scale = W.make_activations(T_EP, seed=0, config="standard", device="cpu")
+    cpu = {"routing_logits": logits, "routing_bias": bias, "hidden_states": hs, "hidden_states_scale": hs_scale,
+           "routed_scaling_factor": 2.5}
+    est = []
+    total = 0.0
+    for i in range(args.warmup + args.steps):
+        e0 = (i * 37 * n_exp) % (E_local - n_exp + 1)
+        w1, s1, w2, s2 = W.make_weights(n_exp, 1000 + e0, "cpu")
+        cpu.update(gemm1_weights=w1, gemm1_weights_scale=s1, gemm2_weights=w2, gemm2_weights_scale=s2)
+        full, used = _sample_block(cpu, {"local_expert_offset": 0}, e0, n_exp, E_local)
+        if i >= args.warmup:
+            est.append(full)
+            total += used
+    call_s = statistics.mean(est)
+    value = T_EP / call_s
+    return {
+        "impl": "reference", "metric": "tokens/s per MoE layer call (DS-V3 FP8 MoE, T=8192, 256 experts, EP over N GPUs)",
+        "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(call_s * 1e3, 1), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 (reference run(): fp32 dequantisation and matmul on CPU)", "data": "synthetic",
+        "config": {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
+                   "parallelism": f"ep{world} (rank 0 shard on host cores)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"each step: {n_exp} of {E_local} experts with all their routed tokens, "
+                                   f"extrapolated x{E_local // n_exp}; {total:.1f} s of CPU work in the timed steps"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("fbmoe", "reference"), default="fbmoe")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for cpu_baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    world, rank, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    line = run_ours(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -38,7 +38,20 @@ enum StatusBits : uint32_t {
   kStatusTimeoutConvert = 1u << 3,
   kStatusBadTile = 1u << 4,
   kStatusTimeoutDrain = 1u << 5,
+  kStatusSaturated = 1u << 6,  // an f16 intermediate/pair value was clamped to +-65504
 };
+
+constexpr float kF16Max = 65504.0f;
+
+// fp32 -> f16 (round to nearest) with saturation; NaN stays NaN.  `sat` is set
+// when a finite value had to be clamped.
+__device__ __forceinline__ __half to_half_sat(float x, bool& sat) {
+  if (fabsf(x) > kF16Max) {
+    sat = true;
+    x = copysignf(kF16Max, x);
+  }
+  return __float2half_rn(x);
+}
 
 // ---------------------------------------------------------------- timing ----
 __device__ __forceinline__ uint64_t globaltimer_ns() {

@@ -20,8 +20,8 @@ struct Layout {
   size_t blocks;       // int4[max_blocks] (expert, row0, nrows, 0)
   size_t row_token;    // int32[pcap]
   size_t row_weight;   // fp32[pcap]
-  size_t inter;        // bf16[pcap * 2048]  SwiGLU output, expert-contiguous rows
-  size_t pair_out;     // bf16[pcap * 7168]  weighted per-(token, expert) rows
+  size_t inter;        // f16[pcap * 2048]   SwiGLU output, expert-contiguous rows
+  size_t pair_out;     // f16[pcap * 7168]   weighted per-(token, expert) rows
   size_t total;        // bytes
   int pcap;            // row capacity (multiple of 128)
   int max_blocks;
@@ -42,11 +42,12 @@ cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const uint8_t* hidden, const 
                          const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
                          cudaStream_t stream);
 
-// GEMM2 (W2 dequantised to bf16 on chip) x routing weight -> pair_out rows.
+// GEMM2 (W2 dequantised to f16 on chip) x routing weight -> pair_out rows.
 cudaError_t launch_gemm2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, const float* w2_scale,
                          int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream);
 
-// out[t, :] = sum of the token's pair rows, fp32 accumulation, bf16 result.
-cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out_bf16, cudaStream_t stream);
+// out[t, :] = sum of the token's pair rows, fp32 accumulation; bf16 result, or
+// fp32 (f32_out) for partial sums that another stage combines across ranks.
+cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, cudaStream_t stream);
 
 }  // namespace fbmoe

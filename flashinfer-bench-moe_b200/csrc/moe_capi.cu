@@ -102,6 +102,22 @@ static int num_sms_of_current_device() {
 
 static int from_cuda(cudaError_t e) { return e == cudaSuccess ? FBMOE_OK : (int)e; }
 
+// Optional stage timing: CUDA events recorded on the forward's stream between
+// the five stages, for up to `cap` forwards (host-side only, no device memory).
+constexpr int kStages = 5;
+struct StageProfile {
+  std::mutex mu;
+  bool on = false;
+  int cap = 0;
+  int n = 0;
+  cudaEvent_t* ev = nullptr;
+};
+static StageProfile g_prof;
+
+static void prof_record(int fwd, int point, cudaStream_t stream) {
+  if (fwd >= 0) cudaEventRecord(g_prof.ev[fwd * (kStages + 1) + point], stream);
+}
+
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 }  // namespace fbmoe
@@ -139,11 +155,11 @@ int fbmoe_route(const float* routing_logits, const void* routing_bias, int T, fl
                                 nullptr, reinterpret_cast<cudaStream_t>(stream)));
 }
 
-int fbmoe_forward(const float* routing_logits, const void* routing_bias, const void* hidden_states,
-                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
-                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
-                  int local_expert_offset, float routed_scaling_factor, void* out, void* workspace,
-                  size_t workspace_bytes, void* stream_) {
+static int forward_impl(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                        const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                        const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                        int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out,
+                        void* workspace, size_t workspace_bytes, void* stream_) {
   if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
   if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale || !gemm1_weights ||
@@ -166,24 +182,109 @@ int fbmoe_forward(const float* routing_logits, const void* routing_bias, const v
   rc = encode_2d(&tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 128,
                  128);
   if (rc) return rc;
-  rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
+  rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
                  (uint32_t)bn);
   if (rc) return rc;
 
+  int fwd = -1;
+  if (g_prof.on) {
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    if (g_prof.on && g_prof.n < g_prof.cap) fwd = g_prof.n++;
+  }
   int32_t* topk_idx = reinterpret_cast<int32_t*>(ws + L.topk_idx);
   float* topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+  prof_record(fwd, 0, stream);
   cudaError_t e = launch_route(routing_logits, routing_bias, T, routed_scaling_factor, topk_idx, topk_w,
                                reinterpret_cast<uint32_t*>(ws + L.status), stream);
   if (e != cudaSuccess) return from_cuda(e);
+  prof_record(fwd, 1, stream);
   e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, L, ws, stream);
   if (e != cudaSuccess) return from_cuda(e);
+  prof_record(fwd, 2, stream);
   e = launch_gemm1(&tm_w1, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
                    gemm1_weights_scale, E_local, bn, L, ws, sms, stream);
   if (e != cudaSuccess) return from_cuda(e);
+  prof_record(fwd, 3, stream);
   e = launch_gemm2(&tm_w2, &tm_inter, gemm2_weights_scale, E_local, bn, L, ws, sms, stream);
   if (e != cudaSuccess) return from_cuda(e);
-  e = launch_reduce(T, L, ws, out, stream);
+  prof_record(fwd, 4, stream);
+  e = launch_reduce(T, L, ws, out, f32_out, stream);
+  prof_record(fwd, 5, stream);
   return from_cuda(e);
+}
+
+int fbmoe_forward(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                  int local_expert_offset, float routed_scaling_factor, void* out, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  return forward_impl(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
+                      routed_scaling_factor, out, false, workspace, workspace_bytes, stream);
+}
+
+int fbmoe_forward_partial_f32(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                              const float* hidden_states_scale, const void* gemm1_weights,
+                              const float* gemm1_weights_scale, const void* gemm2_weights,
+                              const float* gemm2_weights_scale, int T, int E_local, int local_expert_offset,
+                              float routed_scaling_factor, float* out_f32, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  return forward_impl(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
+                      routed_scaling_factor, out_f32, true, workspace, workspace_bytes, stream);
+}
+
+int fbmoe_profile_begin(int max_forwards) {
+  if (max_forwards < 1) return FBMOE_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (g_prof.ev) {
+    for (int i = 0; i < g_prof.cap * (kStages + 1); ++i) cudaEventDestroy(g_prof.ev[i]);
+    delete[] g_prof.ev;
+  }
+  g_prof.ev = new cudaEvent_t[(size_t)max_forwards * (kStages + 1)];
+  for (int i = 0; i < max_forwards * (kStages + 1); ++i) {
+    cudaError_t e = cudaEventCreate(&g_prof.ev[i]);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < i; ++j) cudaEventDestroy(g_prof.ev[j]);
+      delete[] g_prof.ev;
+      g_prof.ev = nullptr;
+      g_prof.cap = 0;
+      return from_cuda(e);
+    }
+  }
+  g_prof.cap = max_forwards;
+  g_prof.n = 0;
+  g_prof.on = true;
+  return FBMOE_OK;
+}
+
+int fbmoe_profile_end(float* stage_ms, int* n_forwards) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.on = false;
+  if (!g_prof.ev) return FBMOE_ERR_INVALID_ARG;
+  int rc = FBMOE_OK;
+  float sums[kStages] = {0, 0, 0, 0, 0};
+  for (int f = 0; f < g_prof.n && rc == FBMOE_OK; ++f) {
+    for (int s = 0; s < kStages; ++s) {
+      cudaEvent_t a = g_prof.ev[f * (kStages + 1) + s], b = g_prof.ev[f * (kStages + 1) + s + 1];
+      cudaError_t e = cudaEventSynchronize(b);
+      float ms = 0.f;
+      if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+      if (e != cudaSuccess) {
+        rc = from_cuda(e);
+        break;
+      }
+      sums[s] += ms;
+    }
+  }
+  if (stage_ms) memcpy(stage_ms, sums, sizeof sums);
+  if (n_forwards) *n_forwards = g_prof.n;
+  for (int i = 0; i < g_prof.cap * (kStages + 1); ++i) cudaEventDestroy(g_prof.ev[i]);
+  delete[] g_prof.ev;
+  g_prof.ev = nullptr;
+  g_prof.cap = 0;
+  g_prof.n = 0;
+  return rc;
 }
 
 int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream_) {

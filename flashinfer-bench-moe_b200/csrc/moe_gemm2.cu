@@ -3,13 +3,15 @@
 //
 // Reference counterpart: gemm2_kernel (Triton, solution/triton/main.py:433-600):
 //     O[r, h] = w[r] * sum_j inter[r, j] * W2[e, h, j] * s2[e, h/128, j/128]
-// written as one bf16 row per (token, local expert) pair.
+// written as one row per (token, local expert) pair.
 //
 // W2 arrives as FP8 with fp32 128x128 block scales.  Because the intermediate
-// is bf16, this GEMM runs as a kind::f16 (bf16 x bf16 -> fp32) MMA: converter
+// is f16, this GEMM runs as a kind::f16 (f16 x f16 -> fp32) MMA: converter
 // warps dequantise each 128x128 W2 tile on chip (fp8 * s2 in fp32, rounded
-// once to bf16) into the UMMA operand layout.  With the scale folded into the
+// once to f16) into the UMMA operand layout.  With the scale folded into the
 // operand no promotion is needed; TMEM accumulates the full K = 2048.
+// The weighted pair rows are written as f16 (clamped to +-65504, flagged) and
+// summed in fp32 by the combine kernel.
 //
 // Orientation (swap-AB): A = 128 rows of W2 (one 128-row scale block of the
 // hidden dimension), B = BN intermediate rows of one expert (TMA, two 64-column
@@ -17,8 +19,13 @@
 // columns); its accumulator is double-buffered in TMEM so the epilogue of one
 // unit overlaps the MMAs of the next.
 //
-// Warp roles (384 threads): w0 producer (TMA), w1 MMA issuer + TMEM owner,
-// w2-w3 idle, w4-w7 converters (one W2 row each), w8-w11 epilogue.
+// Two shared-memory rings: a deep ring of raw FP8 W2 tiles (16 KB each; the
+// bytes that stream from HBM) and a 2-deep ring of converted f16 W2 tiles plus
+// the intermediate rows the MMA reads.
+//
+// Warp roles (384 threads): w0 W2 producer (TMA), w1 MMA issuer + TMEM owner,
+// w2 intermediate producer (TMA), w3 idle, w4-w7 converters (one W2 row each),
+// w8-w11 epilogue.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -31,52 +38,69 @@ constexpr uint64_t kWaitBudgetNs = 4000000000ull;
 
 template <int BN>
 struct G2Cfg {
-  static constexpr int kStages = BN <= 32 ? 4 : 3;
+  static constexpr int kRawStages = BN <= 16 ? 8 : BN <= 32 ? 7 : BN <= 64 ? 6 : 4;
+  static constexpr int kConvStages = 2;
   static constexpr int kRawBytes = 128 * 128;      // fp8 W2 tile
-  static constexpr int kAbfBytes = 2 * 128 * 128;  // bf16 W2 tile (two 64-K halves)
-  static constexpr int kBBytes = BN * 256;         // bf16 intermediate rows (two 64-K halves)
+  static constexpr int kAhBytes = 2 * 128 * 128;   // f16 W2 tile (two 64-K halves)
+  static constexpr int kBBytes = BN * 256;         // f16 intermediate rows (two 64-K halves)
   static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
   static constexpr int kOffRaw = 0;
-  static constexpr int kOffAbf = kOffRaw + kStages * kRawBytes;
-  static constexpr int kOffB = kOffAbf + kStages * kAbfBytes;
-  static constexpr int kOffW = kOffB + kStages * kBBytes;
-  static constexpr int kOffBar = (kOffW + BN * 4 + 7) / 8 * 8;
-  static constexpr int kNumBars = 3 * kStages + 4 + 1;
+  static constexpr int kOffAh = kOffRaw + kRawStages * kRawBytes;
+  static constexpr int kOffB = kOffAh + kConvStages * kAhBytes;
+  static constexpr int kOffBar = kOffB + kConvStages * kBBytes;
+  static constexpr int kNumBars = 2 * kRawStages + 3 * kConvStages + 4 + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16 + 1024;
 };
 
-// 4 fp8 (e4m3) -> 4 bf16, each times `scale` (fp32 multiply, one rounding).
-__device__ __forceinline__ uint2 fp8x4_to_bf16x4(uint32_t q, float scale) {
+// 4 fp8 (e4m3) -> 4 f16, each times `scale` (exact widening, fp32 multiply, one rounding).
+__device__ __forceinline__ uint2 fp8x4_to_f16x4(uint32_t q, float scale) {
   const __half2_raw h01 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(q & 0xFFFFu), __NV_E4M3);
   const __half2_raw h23 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(q >> 16), __NV_E4M3);
   const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
   const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-  const __nv_bfloat162 b01 = __floats2bfloat162_rn(f01.x * scale, f01.y * scale);
-  const __nv_bfloat162 b23 = __floats2bfloat162_rn(f23.x * scale, f23.y * scale);
-  return make_uint2(*reinterpret_cast<const uint32_t*>(&b01), *reinterpret_cast<const uint32_t*>(&b23));
+  const __half2 o01 = __floats2half2_rn(f01.x * scale, f01.y * scale);
+  const __half2 o23 = __floats2half2_rn(f23.x * scale, f23.y * scale);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&o01), *reinterpret_cast<const uint32_t*>(&o23));
 }
+
+// Ring position: slot and phase parity of successive uses of a ring of n slots.
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  int n;
+  __device__ explicit Ring(int n_) : n(n_) {}
+  __device__ void next() {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
 
 template <int BN>
 __global__ void __launch_bounds__(kG2Threads, 1)
     gemm2_combine_kernel(const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_inter,
                          const float* __restrict__ w2_scale, const int32_t* __restrict__ n_blocks_ptr,
                          const int4* __restrict__ blocks, const float* __restrict__ row_weight,
-                         __nv_bfloat16* __restrict__ pair_out, uint32_t* __restrict__ status) {
+                         __half* __restrict__ pair_out, uint32_t* __restrict__ status) {
   using C = G2Cfg<BN>;
-  constexpr int S = C::kStages;
+  constexpr int SR = C::kRawStages;
+  constexpr int SC = C::kConvStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sRaw = sm + C::kOffRaw;
-  uint8_t* sAbf = sm + C::kOffAbf;
+  uint8_t* sAh = sm + C::kOffAh;
   uint8_t* sB = sm + C::kOffB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
-  uint64_t* full = bars;            // TMA landed (raw W2 + B)
-  uint64_t* conv = bars + S;        // bf16 W2 written
-  uint64_t* empty = bars + 2 * S;   // MMA done with the stage
-  uint64_t* tfull = bars + 3 * S;
-  uint64_t* tempty = bars + 3 * S + 2;
-  uint64_t* drain = bars + 3 * S + 4;
+  uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
+  uint64_t* raw_empty = bars + SR;             // converters done reading it
+  uint64_t* b_full = bars + 2 * SR;            // intermediate rows landed (TMA)
+  uint64_t* a_full = bars + 2 * SR + SC;       // f16 W2 tile written by the converters
+  uint64_t* c_empty = bars + 2 * SR + 2 * SC;  // MMA done with the converted slot
+  uint64_t* tfull = bars + 2 * SR + 3 * SC;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tfull + 4;
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + C::kOffMisc);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sm + C::kOffMisc + 4);
 
@@ -84,10 +108,14 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SR; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 4);
+    }
+    for (int s = 0; s < SC; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&a_full[s], 4);
+      mbar_init(&c_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -116,49 +144,53 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     atomicOr(status, bit);
   };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ producers
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_a = l2_policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
+      const bool w2_side = (warp == 0);
+      const uint64_t pol = w2_side ? l2_policy_evict_first() : l2_policy_evict_last();
+      const int n = w2_side ? SR : SC;
+      uint64_t* fullb = w2_side ? raw_full : b_full;
+      uint64_t* emptyb = w2_side ? raw_empty : c_empty;
+      Ring ring(n);
       bool ok = true;
-      uint32_t last_parity[S];
-      for (int s = 0; s < S; ++s) last_parity[s] = 0xFFFFFFFFu;
+      uint32_t last_parity[SR > SC ? SR : SC];
+      for (int s = 0; s < n; ++s) last_parity[s] = 0xFFFFFFFFu;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const int4 blk = blocks[u / kG2Slices];
         const int h = u % kG2Slices;
         const int e = blk.x, r0 = blk.y;
         for (int kb = 0; kb < kIBlocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
+          if (!mbar_wait(&emptyb[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutProducer);
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::kRawBytes + C::kBBytes);
-          tma_load_2d(sRaw + stage * C::kRawBytes, &tm_w2, &full[stage], kb * kBlk, e * kHidden + h * 128, pol_w);
-          uint8_t* b = sB + stage * C::kBBytes;
-          tma_load_2d(b, &tm_inter, &full[stage], kb * kBlk, r0, pol_a);
-          tma_load_2d(b + BN * 128, &tm_inter, &full[stage], kb * kBlk + 64, r0, pol_a);
-          last_parity[stage] = phase;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
+          if (w2_side) {
+            mbar_arrive_expect_tx(&fullb[ring.slot], C::kRawBytes);
+            tma_load_2d(sRaw + ring.slot * C::kRawBytes, &tm_w2, &fullb[ring.slot], kb * kBlk,
+                        e * kHidden + h * 128, pol);
+          } else {
+            uint8_t* b = sB + ring.slot * C::kBBytes;
+            mbar_arrive_expect_tx(&fullb[ring.slot], C::kBBytes);
+            tma_load_2d(b, &tm_inter, &fullb[ring.slot], kb * kBlk, r0, pol);
+            tma_load_2d(b + BN * 128, &tm_inter, &fullb[ring.slot], kb * kBlk + 64, r0, pol);
           }
+          last_parity[ring.slot] = ring.phase;
+          ring.next();
         }
       }
-      for (int s = 0; s < S; ++s)
+      // every issued TMA load lands before the CTA exits
+      for (int s = 0; s < n; ++s)
         if (last_parity[s] != 0xFFFFFFFFu)
-          if (!mbar_wait(&full[s], last_parity[s], sAbort, kWaitBudgetNs) && !*sAbort) fail(kStatusTimeoutDrain);
+          if (!mbar_wait(&fullb[s], last_parity[s], sAbort, kWaitBudgetNs) && !*sAbort) fail(kStatusTimeoutDrain);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc(1u, 128, BN);  // bf16 x bf16
-      int stage = 0;
-      uint32_t phase = 0;
+      constexpr uint32_t idesc = umma_idesc(0u, 128, BN);  // f16 x f16
+      Ring ring(SC);
       uint32_t ug = 0;
       bool ok = true;
       bool any = false;
@@ -172,8 +204,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         for (int kb = 0; kb < kIBlocks; ++kb) {
-          if (!mbar_wait(&conv[stage], phase, sAbort, kWaitBudgetNs) ||
-              !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
+          if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs) ||
+              !mbar_wait(&b_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
@@ -181,18 +213,15 @@ __global__ void __launch_bounds__(kG2Threads, 1)
           tc_fence_after();
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
-            const uint64_t adesc = umma_desc_sw128(smem_u32(sAbf + stage * C::kAbfBytes + half * 128 * 128));
-            const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * C::kBBytes + half * BN * 128));
+            const uint64_t adesc = umma_desc_sw128(smem_u32(sAh + ring.slot * C::kAhBytes + half * 128 * 128));
+            const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + ring.slot * C::kBBytes + half * BN * 128));
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               mma_f16(d, adesc + 2 * j, bdesc + 2 * j, idesc, (kb | half | j) ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          tc_commit(&c_empty[ring.slot]);
           any = true;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          ring.next();
         }
         if (!ok) break;
         tc_commit(&tfull[buf]);
@@ -206,41 +235,42 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ converters
     const int r = threadIdx.x - 128;  // W2 row within the tile
-    int stage = 0;
-    uint32_t phase = 0;
+    Ring rr(SR), cr(SC);
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const int4 blk = blocks[u / kG2Slices];
       const int h = u % kG2Slices;
       const float* sc = w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
       for (int kb = 0; kb < kIBlocks; ++kb) {
-        if (!mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
+        if (!mbar_wait(&raw_full[rr.slot], rr.phase, sAbort, kWaitBudgetNs) ||
+            !mbar_wait(&c_empty[cr.slot], cr.phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutConvert);
           break;
         }
         const float scale = __ldg(sc + kb);
-        const uint8_t* raw = sRaw + stage * C::kRawBytes;
-        uint8_t* abf = sAbf + stage * C::kAbfBytes;
+        const uint8_t* raw = sRaw + rr.slot * C::kRawBytes;
+        uint8_t* ah = sAh + cr.slot * C::kAhBytes;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint4 q = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, c));
-          const uint2 o0 = fp8x4_to_bf16x4(q.x, scale);
-          const uint2 o1 = fp8x4_to_bf16x4(q.y, scale);
-          const uint2 o2 = fp8x4_to_bf16x4(q.z, scale);
-          const uint2 o3 = fp8x4_to_bf16x4(q.w, scale);
-          uint8_t* dst = abf + (c >> 2) * (128 * 128);
+          const uint2 o0 = fp8x4_to_f16x4(q.x, scale);
+          const uint2 o1 = fp8x4_to_f16x4(q.y, scale);
+          const uint2 o2 = fp8x4_to_f16x4(q.z, scale);
+          const uint2 o3 = fp8x4_to_f16x4(q.w, scale);
+          uint8_t* dst = ah + (c >> 2) * (128 * 128);
           const int c2 = (c & 3) * 2;
           *reinterpret_cast<uint4*>(dst + sw128_offset(r, c2)) = make_uint4(o0.x, o0.y, o1.x, o1.y);
           *reinterpret_cast<uint4*>(dst + sw128_offset(r, c2 + 1)) = make_uint4(o2.x, o2.y, o3.x, o3.y);
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[stage]);
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+        if (lane == 0) {
+          mbar_arrive(&raw_empty[rr.slot]);
+          mbar_arrive(&a_full[cr.slot]);
         }
+        rr.next();
+        cr.next();
       }
     }
   } else if (warp >= 8) {
@@ -261,8 +291,9 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         break;
       }
       tc_fence_after();
-      __nv_bfloat16* dst = pair_out + (size_t)r0 * kHidden + h * 128 + hrow;
+      __half* dst = pair_out + (size_t)r0 * kHidden + h * 128 + hrow;
       const float* wrow = row_weight + r0;
+      bool sat = false;
 #pragma unroll
       for (int c = 0; c < BN / 16; ++c) {
         float p[16];
@@ -271,12 +302,13 @@ __global__ void __launch_bounds__(kG2Threads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int t = c * 16 + i;
-          if (t < nrows) dst[(size_t)t * kHidden] = __float2bfloat16_rn(p[i] * __ldg(wrow + t));
+          if (t < nrows) dst[(size_t)t * kHidden] = to_half_sat(p[i] * __ldg(wrow + t), sat);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (sat) atomicOr(status, kStatusSaturated);
     }
   }
 
@@ -292,6 +324,7 @@ template <int BN>
 cudaError_t launch_g2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, const float* w2_scale,
                       const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream) {
   using C = G2Cfg<BN>;
+  static_assert(C::kBytes <= 227 * 1024, "GEMM2 shared memory over the per-CTA limit");
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -307,7 +340,7 @@ cudaError_t launch_g2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, con
   gemm2_combine_kernel<BN><<<grid, kG2Threads, C::kBytes, stream>>>(
       *tm_w2, *tm_inter, w2_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
       reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const float*>(ws + L.row_weight),
-      reinterpret_cast<__nv_bfloat16*>(ws + L.pair_out), reinterpret_cast<uint32_t*>(ws + L.status));
+      reinterpret_cast<__half*>(ws + L.pair_out), reinterpret_cast<uint32_t*>(ws + L.status));
   return cudaGetLastError();
 }
 

@@ -1,9 +1,9 @@
 // moe_reduce.cu -- per-token combine of the weighted (token, expert) rows.
 //
 // Reference counterpart: reduce_add_kernel_small/large (solution/triton/main.py:
-// 1604-1714), which adds the pair rows with bf16 __hadd2.  Here the sum runs in
-// fp32 over the token's slots in fixed slot order (deterministic) and is rounded
-// to bf16 once.  Tokens with no local expert get a zero row, as in the reference.
+// 1604-1714), which adds bf16 pair rows with bf16 __hadd2.  Here the f16 pair
+// rows are summed in fp32 over the token's slots in fixed slot order
+// (deterministic) and rounded to bf16 once.  Tokens with no local expert get a zero row, as in the reference.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -13,9 +13,10 @@ namespace {
 constexpr int kReduceThreads = 128;               // 128 threads x 8 bf16 = 1024 columns
 constexpr int kReduceChunks = kHidden / (kReduceThreads * 8);  // 7
 
-__global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __nv_bfloat16* __restrict__ pair_out,
+template <bool kF32Out>
+__global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __restrict__ pair_out,
                                                                 const int32_t* __restrict__ token_rows,
-                                                                __nv_bfloat16* __restrict__ out) {
+                                                                void* __restrict__ out_) {
   const int t = blockIdx.y;
   const int col = (blockIdx.x * kReduceThreads + threadIdx.x) * 8;
   float acc[8];
@@ -31,29 +32,39 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __nv_bfloa
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        acc[2 * i] += __uint_as_float(w[i] << 16);
-        acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
       }
     }
   }
-  uint4 o;
-  uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+  if constexpr (kF32Out) {
+    float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out_) + (size_t)t * kHidden + col);
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  } else {
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-    ow[i] = *reinterpret_cast<const uint32_t*>(&b);
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      ow[i] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out_) + (size_t)t * kHidden + col) = o;
   }
-  *reinterpret_cast<uint4*>(out + (size_t)t * kHidden + col) = o;
 }
 
 }  // namespace
 
-cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out_bf16, cudaStream_t stream) {
+cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   dim3 grid(kReduceChunks, T);
-  reduce_kernel<<<grid, kReduceThreads, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(ws + L.pair_out),
-                                                     reinterpret_cast<const int32_t*>(ws + L.token_rows),
-                                                     reinterpret_cast<__nv_bfloat16*>(out_bf16));
+  const __half* pairs = reinterpret_cast<const __half*>(ws + L.pair_out);
+  const int32_t* rows = reinterpret_cast<const int32_t*>(ws + L.token_rows);
+  if (f32_out)
+    reduce_kernel<true><<<grid, kReduceThreads, 0, stream>>>(pairs, rows, out);
+  else
+    reduce_kernel<false><<<grid, kReduceThreads, 0, stream>>>(pairs, rows, out);
   return cudaGetLastError();
 }
 

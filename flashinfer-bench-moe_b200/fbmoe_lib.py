@@ -49,6 +49,13 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_workspace_size.restype = sz
         lib.fbmoe_forward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, sz, vp]
         lib.fbmoe_forward.restype = i32
+        lib.fbmoe_forward_partial_f32.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, sz,
+                                                  vp]
+        lib.fbmoe_forward_partial_f32.restype = i32
+        lib.fbmoe_profile_begin.argtypes = [i32]
+        lib.fbmoe_profile_begin.restype = i32
+        lib.fbmoe_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int)]
+        lib.fbmoe_profile_end.restype = i32
         lib.fbmoe_route.argtypes = [vp, vp, i32, f32, vp, vp, vp]
         lib.fbmoe_route.restype = i32
         lib.fbmoe_workspace_layout.argtypes = [i32, i32, ctypes.POINTER(ctypes.c_int64)]
@@ -152,8 +159,12 @@ def check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scal
 
 def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
             gemm2_weights, gemm2_weights_scale, local_expert_offset, routed_scaling_factor,
-            out: torch.Tensor = None, workspace: torch.Tensor = None, check: bool = True) -> torch.Tensor:
-    """Run the fused MoE on the current stream; returns bf16 [T, 7168] (a fresh tensor unless `out` is given)."""
+            out: torch.Tensor = None, workspace: torch.Tensor = None, check: bool = True,
+            partial_f32: bool = False) -> torch.Tensor:
+    """Run the fused MoE on the current stream; returns bf16 [T, 7168] (a fresh tensor unless `out` is given).
+
+    With ``partial_f32`` the un-rounded fp32 sum over the local experts is returned
+    instead (the expert-parallel partial)."""
     lib = load_library()
     if check:
         T, E = check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
@@ -161,20 +172,39 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
     else:
         T, E = hidden_states.size(0), gemm1_weights.size(0)
     dev = hidden_states.device
+    out_dtype = torch.float32 if partial_f32 else torch.bfloat16
     if out is None:
-        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((T, H), dtype=out_dtype, device=dev)
+    _require(out.dtype == out_dtype and out.is_contiguous() and tuple(out.shape) == (T, H), "bad `out` tensor")
     if T == 0:
         return out
     stream = torch.cuda.current_stream(dev).cuda_stream
     need = int(lib.fbmoe_workspace_size(T, E))
     if workspace is None:
         workspace = get_workspace(need, dev, stream)
-    _check(lib.fbmoe_forward(
+    fn = lib.fbmoe_forward_partial_f32 if partial_f32 else lib.fbmoe_forward
+    _check(fn(
         routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
         gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(), gemm2_weights.data_ptr(),
         gemm2_weights_scale.data_ptr(), int(T), int(E), int(local_expert_offset), float(routed_scaling_factor),
         out.data_ptr(), workspace.data_ptr(), int(workspace.numel()), stream))
     return out
+
+
+def profile_begin(max_forwards: int) -> None:
+    """Record per-stage CUDA events for the next `max_forwards` forwards."""
+    _check(load_library().fbmoe_profile_begin(int(max_forwards)))
+
+
+def profile_end():
+    """(summed ms per stage [route, permute, gemm1, gemm2, combine], number of forwards)."""
+    ms = (ctypes.c_float * 5)()
+    n = ctypes.c_int(0)
+    _check(load_library().fbmoe_profile_end(ms, ctypes.byref(n)))
+    return [float(x) for x in ms], int(n.value)
+
+
+STAGES = ("route", "permute", "gemm1", "gemm2", "combine")
 
 
 def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, routed_scaling_factor: float):

@@ -71,6 +71,17 @@ FBMOE_API int fbmoe_forward(const float* routing_logits, const void* routing_bia
                   int local_expert_offset, float routed_scaling_factor, void* out, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Same as fbmoe_forward but writes the un-rounded fp32 sum over the local experts
+ * (out_f32 [T, 7168]) -- the partial that expert-parallel ranks add together
+ * before the single bf16 rounding.  No reference counterpart (the reference
+ * leaves combining ranks to its caller, main.py:2452-2455). */
+FBMOE_API int fbmoe_forward_partial_f32(const float* routing_logits, const void* routing_bias,
+                                        const void* hidden_states, const float* hidden_states_scale,
+                                        const void* gemm1_weights, const float* gemm1_weights_scale,
+                                        const void* gemm2_weights, const float* gemm2_weights_scale, int T,
+                                        int E_local, int local_expert_offset, float routed_scaling_factor,
+                                        float* out_f32, void* workspace, size_t workspace_bytes, void* stream);
+
 /* DeepSeek-V3 no-aux routing only (reference main.py:2522-2553 / fusedGatingKernel
  * main.py:851-1038).  topk_idx int32 [T, 8] global expert ids in canonical order
  * (descending s+bias, ascending id among equals); topk_weights fp32 [T, 8]. */
@@ -92,6 +103,15 @@ FBMOE_API int fbmoe_block_rows(int T, int E_local);
  * a kernel (bit 0 producer, 1 MMA, 2 epilogue, 3 converter, 5 drain) or the
  * block list overflowed (bit 4). */
 FBMOE_API int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream);
+
+/* Stage timing for measurement: after fbmoe_profile_begin(n), the next n
+ * forwards record CUDA events on their stream between the stages (route,
+ * permute, GEMM1, GEMM2, combine).  fbmoe_profile_end synchronises those events,
+ * writes the summed milliseconds per stage to stage_ms[5] and the number of
+ * recorded forwards, and stops recording.  Host-side only (events, no device
+ * memory); the reference has wall-clock timing only (main.py:2611-2624). */
+FBMOE_API int fbmoe_profile_begin(int max_forwards);
+FBMOE_API int fbmoe_profile_end(float* stage_ms, int* n_forwards);
 
 FBMOE_API const char* fbmoe_error_string(int code);
 

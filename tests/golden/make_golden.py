@@ -36,7 +36,7 @@ import fbmoe_workloads as W  # noqa: E402
 
 def tensor_checksum(t: torch.Tensor) -> str:
     """Order-sensitive 64-bit checksum of a tensor's bytes (fast, numpy-vectorised)."""
-    b = t.detach().cpu().contiguous().view(torch.uint8).numpy().reshape(-1)
+    b = t.detach().cpu().reshape(-1).clone().view(torch.uint8).numpy()
     pad = (-b.size) % 8
     if pad:
         b = np.concatenate([b, np.zeros(pad, dtype=np.uint8)])
@@ -116,6 +116,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--only", default="")
+    ap.add_argument("--cases", default="", help="comma-separated moe case names (default: all)")
     args = ap.parse_args()
     run, ref_route = load_reference(args.reference)
     torch.set_num_threads(os.cpu_count())
@@ -132,7 +133,10 @@ def main():
 
     if args.only in ("", "moe"):
         weight_cache = {}
+        wanted = set(filter(None, args.cases.split(",")))
         for name, T, cfg, seed, off, wseed, scale in MOE_CASES:
+            if wanted and name not in wanted:
+                continue
             if wseed not in weight_cache:
                 t0 = time.time()
                 weight_cache[wseed] = W.make_weights(32, wseed, "cpu")
