@@ -426,6 +426,38 @@ def run_reference(args, world, rank):
     }
 
 
+def run_case(args):
+    """One config at one T on GPU 0 (used for profiling captures): decode = config 1,
+    prefill = config 2 (skewed routing); 32 local experts, L2 flushed between calls."""
+    import fbmoe_lib as L
+    import fbmoe_workloads as W
+    torch.cuda.set_device(0)
+    peaks = load_peaks()
+    weights = W.make_weights(32, 4242, "cuda")
+    inp = W.make_inputs(args.T, seed=args.T, config="standard" if args.case == "decode" else "skew",
+                        device="cuda", weights=weights)
+    fargs = W.as_args(inp)
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        L.forward(*fargs, check=False)
+    ts = []
+    for _ in range(args.steps):
+        flush_l2(buf)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        L.forward(*fargs, check=False)
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    pairs, active = local_pairs(inp, 32, 0)
+    ms = statistics.median(ts)
+    nbytes = active * BYTES_PER_EXPERT + BYTES_PER_TOKEN * args.T + 512
+    print(json.dumps({"case": args.case, "T": args.T, "us_per_call": round(ms * 1e3, 2), "local_pairs": pairs,
+                      "active_experts": active, "hbm_gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                      "tflops": round(pairs * FLOPS_PER_PAIR / (ms / 1e3) / 1e12, 1),
+                      "peak_hbm_gbs": peaks["hbm_gbs"]}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -435,9 +467,15 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for cpu_baseline")
+    ap.add_argument("--case", choices=("ep", "decode", "prefill"), default="ep",
+                    help="ep = the benchmark line (default); decode/prefill = one small config for profiling")
+    ap.add_argument("--T", type=int, default=64, help="tokens for --case decode/prefill")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.case != "ep":
+        run_case(args)
+        return
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
