@@ -50,4 +50,12 @@ cudaError_t launch_gemm2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, 
 // fp32 (f32_out) for partial sums that another stage combines across ranks.
 cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, cudaStream_t stream);
 
+// The whole forward on a caller-provided workspace (argument checks, TMA
+// descriptors, the five launches); the public entry points wrap it.
+int forward_core(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                 const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                 const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                 int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 }  // namespace fbmoe

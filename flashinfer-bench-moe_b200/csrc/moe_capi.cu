@@ -155,7 +155,10 @@ int fbmoe_route(const float* routing_logits, const void* routing_bias, int T, fl
                                 nullptr, reinterpret_cast<cudaStream_t>(stream)));
 }
 
-static int forward_impl(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+}  // extern "C"
+
+namespace fbmoe {
+int forward_core(const float* routing_logits, const void* routing_bias, const void* hidden_states,
                         const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
                         const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                         int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out,
@@ -213,12 +216,16 @@ static int forward_impl(const float* routing_logits, const void* routing_bias, c
   return from_cuda(e);
 }
 
+}  // namespace fbmoe
+
+extern "C" {
+
 int fbmoe_forward(const float* routing_logits, const void* routing_bias, const void* hidden_states,
                   const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
                   const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                   int local_expert_offset, float routed_scaling_factor, void* out, void* workspace,
                   size_t workspace_bytes, void* stream) {
-  return forward_impl(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+  return forward_core(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
                       routed_scaling_factor, out, false, workspace, workspace_bytes, stream);
 }
@@ -229,7 +236,7 @@ int fbmoe_forward_partial_f32(const float* routing_logits, const void* routing_b
                               const float* gemm2_weights_scale, int T, int E_local, int local_expert_offset,
                               float routed_scaling_factor, float* out_f32, void* workspace, size_t workspace_bytes,
                               void* stream) {
-  return forward_impl(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+  return forward_core(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
                       routed_scaling_factor, out_f32, true, workspace, workspace_bytes, stream);
 }
@@ -305,6 +312,7 @@ const char* fbmoe_error_string(int code) {
     case FBMOE_ERR_MISALIGNED: return "misaligned pointer (tensors need 16-byte, workspace 256-byte alignment)";
     case FBMOE_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected a tensor map";
     case FBMOE_ERR_DEVICE_STATUS: return "a kernel reported a device-side error (bounded wait expired)";
+    case FBMOE_ERR_NOALLOC_LIMIT: return "fbmoe_forward_noalloc supports T <= 16 and E_local <= 32 only";
     default: break;
   }
   if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));

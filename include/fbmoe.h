@@ -45,6 +45,7 @@ extern "C" {
 #define FBMOE_ERR_MISALIGNED (-4)
 #define FBMOE_ERR_DRIVER (-5)
 #define FBMOE_ERR_DEVICE_STATUS (-6)
+#define FBMOE_ERR_NOALLOC_LIMIT (-7)
 
 /* Bytes of device workspace fbmoe_forward needs for T tokens and E_local local
  * experts (the reference sizes one global workspace for 15000 tokens,
@@ -81,6 +82,24 @@ FBMOE_API int fbmoe_forward_partial_f32(const float* routing_logits, const void*
                                         const void* gemm2_weights, const float* gemm2_weights_scale, int T,
                                         int E_local, int local_expert_offset, float routed_scaling_factor,
                                         float* out_f32, void* workspace, size_t workspace_bytes, void* stream);
+
+/* fbmoe_forward for callers that cannot allocate device memory (no counterpart
+ * in the reference).  Such callers -- a plugin host that hands over only input
+ * and output pointers, a runtime whose allocator may not be called on this
+ * path -- cannot supply the workspace fbmoe_forward needs, so this entry point
+ * keeps it in a fixed 12 MiB device array inside the library instead.  Limits:
+ * T <= 16 and E_local <= 32 (decode batches of one 32-expert shard); larger
+ * sizes return FBMOE_ERR_NOALLOC_LIMIT.  The array exists on every GPU where the
+ * library's device code is loaded, until the process exits.  Every call shares
+ * it: calls that overlap on the GPU (e.g. on two streams) race.  The first call
+ * on a device looks up the array's address (cudaGetSymbolAddress) with that
+ * device current; make it before any stream capture.  No call allocates or
+ * frees device memory. */
+FBMOE_API int fbmoe_forward_noalloc(const float* routing_logits, const void* routing_bias,
+                                    const void* hidden_states, const float* hidden_states_scale,
+                                    const void* gemm1_weights, const float* gemm1_weights_scale,
+                                    const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                                    int local_expert_offset, float routed_scaling_factor, void* out, void* stream);
 
 /* DeepSeek-V3 no-aux routing only (reference main.py:2522-2553 / fusedGatingKernel
  * main.py:851-1038).  topk_idx int32 [T, 8] global expert ids in canonical order
