@@ -22,12 +22,21 @@ struct Layout {
   size_t row_weight;   // fp32[pcap]
   size_t inter;        // f16[pcap * 2048]   SwiGLU output, expert-contiguous rows
   size_t pair_out;     // f16[pcap * 7168]   weighted per-(token, expert) rows
+  size_t a_perm;       // e4m3[pcap * 7168]  token rows in permuted order (128-row blocks only)
+  size_t a_scale_perm; // fp32[pcap * 56]    their 1x128 scales, row-major (128-row blocks only)
   size_t total;        // bytes
   int pcap;            // row capacity (multiple of 128)
+  int e_local;         // local experts the layout was made for
   int max_blocks;
 };
 
 Layout make_layout(int T, int E_local);
+int choose_block_rows(int T, int E_local);
+
+// Copies each routed token's row (and its 56 scales, row-major) to its permuted
+// position, for the 128-row-block GEMM1 that loads A with plain TMA boxes.
+cudaError_t launch_gather_rows(const uint8_t* hidden, const float* hidden_scale, int T, const Layout& L,
+                               uint8_t* ws, cudaStream_t stream);
 
 // Router: topk_idx/topk_w for T tokens; zeroes status[0].
 cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, float scale, int32_t* topk_idx,
@@ -38,13 +47,24 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
                            int bn, const Layout& L, uint8_t* ws, cudaStream_t stream);
 
 // GEMM1 + SwiGLU: inter[row, :] for every local (token, expert) row.
-cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const uint8_t* hidden, const float* hidden_scale, int T,
+// tm_aperm: the permuted activation rows (a_perm) in 128-row boxes (used for block_rows 128).
+cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const uint8_t* hidden, const float* hidden_scale, int T,
                          const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
                          cudaStream_t stream);
+
+// GEMM1 + SwiGLU for blocks of 128 rows with the tokens as the MMA M operand.
+cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const float* a_scale_perm,
+                              const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
+                              cudaStream_t stream);
 
 // GEMM2 (W2 dequantised to f16 on chip) x routing weight -> pair_out rows.
 cudaError_t launch_gemm2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, const float* w2_scale,
                          int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream);
+
+// GEMM2 for blocks of 128 rows with the tokens as the MMA M operand; tm_w2raw
+// maps W2 as unswizzled 64-byte x 256-row boxes.
+cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
+                              const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream);
 
 // out[t, :] = sum of the token's pair rows, fp32 accumulation; bf16 result, or
 // fp32 (f32_out) for partial sums that another stage combines across ranks.

@@ -13,13 +13,21 @@
 
 #include <mutex>
 
-#include "../../include/fbmoe.h"
+#include "fbmoe.h"
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
 namespace fbmoe {
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int choose_block_rows(int T, int E_local) {
+  (void)E_local;
+  if (T <= 256) return 16;
+  if (T <= 1024) return 32;
+  if (T <= 4096) return 64;
+  return 128;
+}
 
 Layout make_layout(int T, int E_local) {
   Layout L;
@@ -48,17 +56,14 @@ Layout make_layout(int T, int E_local) {
   L.row_weight = take((size_t)pcap * 4);
   L.inter = take((size_t)pcap * kInter * 2);
   L.pair_out = take((size_t)pcap * kHidden * 2);
+  const bool big = choose_block_rows(T, E_local) == 128;
+  L.a_perm = take(big ? (size_t)pcap * kHidden : 0);
+  L.a_scale_perm = take(big ? (size_t)pcap * kHBlocks * 4 : 0);
+  L.e_local = el;
   L.total = off;
   return L;
 }
 
-static int choose_block_rows(int T, int E_local) {
-  (void)E_local;
-  if (T <= 256) return 16;
-  if (T <= 1024) return 32;
-  if (T <= 4096) return 64;
-  return 128;
-}
 
 // ---------------------------------------------------------------- driver ----
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -75,16 +80,17 @@ static bool get_encode() {
   return g_encode != nullptr;
 }
 
-// 2-D K-major tile map with 128-byte swizzle.  inner = K extent (elements).
+// 2-D K-major tile map (128-byte swizzle unless stated).  inner = K extent (elements).
 static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
-                     uint64_t rows, uint32_t box_inner, uint32_t box_rows) {
+                     uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   if (!get_encode()) return FBMOE_ERR_DRIVER;
   const cuuint64_t dims[2] = {inner, rows};
   const cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
   const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FBMOE_OK : FBMOE_ERR_DRIVER;
 }
@@ -178,12 +184,20 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   const int bn = choose_block_rows(T, E_local);
   const int sms = num_sms_of_current_device();
 
-  CUtensorMap tm_w1, tm_w2, tm_inter;
+  CUtensorMap tm_w1, tm_w2, tm_inter, tm_w2raw, tm_aperm;
   int rc = encode_2d(&tm_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm1_weights, kHidden, (uint64_t)E_local * kGemm1N,
                      128, 64);
   if (rc) return rc;
   rc = encode_2d(&tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 128,
                  128);
+  if (rc) return rc;
+  if (bn == 128) {
+    rc = encode_2d(&tm_aperm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + L.a_perm, kHidden, (uint64_t)L.pcap, 128, 128);
+    if (rc) return rc;
+  }
+  // W2 in 64-byte (64-K) slices of 256 rows, unswizzled: converted on chip by GEMM2.
+  rc = encode_2d(&tm_w2raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 64,
+                 256, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
                  (uint32_t)bn);
@@ -204,11 +218,16 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, L, ws, stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 2, stream);
-  e = launch_gemm1(&tm_w1, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
+  if (bn == 128) {
+    e = launch_gather_rows(reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, L, ws, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+  }
+  e = launch_gemm1(&tm_w1, &tm_aperm, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
                    gemm1_weights_scale, E_local, bn, L, ws, sms, stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 3, stream);
-  e = launch_gemm2(&tm_w2, &tm_inter, gemm2_weights_scale, E_local, bn, L, ws, sms, stream);
+  e = bn == 128 ? launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream)
+                : launch_gemm2(&tm_w2, &tm_inter, gemm2_weights_scale, E_local, bn, L, ws, sms, stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 4, stream);
   e = launch_reduce(T, L, ws, out, f32_out, stream);

@@ -66,6 +66,9 @@ __global__ void __launch_bounds__(kG1Threads, 1)
                         uint32_t* __restrict__ status) {
   using C = G1Cfg<BN>;
   constexpr int S = C::kStages;
+  // Decode-sized blocks read each weight tile about once: stream it past L2.
+  // Larger blocks mean several token blocks per expert reuse the tile from L2.
+  constexpr bool kStreamWeights = (BN <= 16);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = sm + C::kOffA;
@@ -148,8 +151,13 @@ __global__ void __launch_bounds__(kG1Threads, 1)
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[stage], C::kABytes);
-          tma_load_2d(sA + stage * C::kABytes, &tm_w1, &full[stage], kb * kBlk, wrow1, pol_w);
-          tma_load_2d(sA + stage * C::kABytes + 64 * 128, &tm_w1, &full[stage], kb * kBlk, wrow2, pol_w);
+          if (kStreamWeights) {
+            tma_load_2d(sA + stage * C::kABytes, &tm_w1, &full[stage], kb * kBlk, wrow1, pol_w);
+            tma_load_2d(sA + stage * C::kABytes + 64 * 128, &tm_w1, &full[stage], kb * kBlk, wrow2, pol_w);
+          } else {
+            tma_load_2d_nohint(sA + stage * C::kABytes, &tm_w1, &full[stage], kb * kBlk, wrow1);
+            tma_load_2d_nohint(sA + stage * C::kABytes + 64 * 128, &tm_w1, &full[stage], kb * kBlk, wrow2);
+          }
         }
         last_parity[stage] = phase;
         const uint32_t bdst = smem_u32(sB + stage * C::kBBytes);
@@ -347,7 +355,7 @@ cudaError_t launch_g1(const CUtensorMap* tm, const uint8_t* hidden, const float*
 
 }  // namespace
 
-cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const uint8_t* hidden, const float* hidden_scale, int T,
+cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const uint8_t* hidden, const float* hidden_scale, int T,
                          const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
                          cudaStream_t stream) {
   (void)E_local;
@@ -355,7 +363,9 @@ cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const uint8_t* hidden, const 
     case 16: return launch_g1<16>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
     case 32: return launch_g1<32>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
     case 64: return launch_g1<64>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
-    case 128: return launch_g1<128>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
+    case 128:
+      return launch_gemm1_rows(tm_w1, tm_aperm, reinterpret_cast<const float*>(ws + L.a_scale_perm), w1_scale, L, ws,
+                               num_sms, stream);
     default: return cudaErrorInvalidValue;
   }
 }

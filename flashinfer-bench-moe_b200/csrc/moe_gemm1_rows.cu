@@ -1,0 +1,292 @@
+// moe_gemm1_rows.cu -- GEMM1 + SwiGLU for large token blocks (prefill), with
+// the tokens as the MMA's M operand (tcgen05 kind::f8f6f4, TMEM, TMA), sm_100a.
+//
+// Same result as moe_gemm1.cu (reference gemm1_kernel + act_quant_kernel,
+// solution/triton/main.py:41-223, 1426-1602): per permuted row r (token t) of
+// expert e,
+//     G1[r, n] = sum_k A[t, k] * a_scale[k/128, t] * W1[e, n, k] * s1[e, n/128, k/128]
+//     inter[r, j] = silu(G1[r, 2048 + j]) * G1[r, j]      (f16, clamped to +-65504)
+//
+// Orientation.  A = 128 token rows (one block of the permuted list), read by TMA
+// as one 128 x 128-byte box from the permuted copy of the activations (see
+// moe_gather.cu for why the rows are copied first); B = 256 W1 rows: the 128 rows of one scale
+// block of the first half stacked on the matching 128 rows of the second half
+// (TMA).  D = 128 x 256 fp32 in TMEM.  Each thread of the epilogue owns one token
+// row, so the per-128-K promotion is ONE multiply-add per element with a
+// per-thread factor (a_scale[row] * s1[block]) instead of a per-column factor,
+// and SwiGLU pairs columns c and 128 + c inside a thread.
+//
+// One work unit = (block of <=128 rows) x (tile j of 128 intermediate columns),
+// 56 K-blocks.  Each K-block is MMA'd into one of two 256-column TMEM buffers
+// (all 512 columns) while the epilogue promotes the other.
+//
+// Warp roles (576 threads): w0 producer (TMA for the activation and W1 tiles),
+// w1 MMA issuer + TMEM owner, w2-w17 epilogue: 16 warps, four per SM
+// sub-partition so that their TMEM-load latencies overlap; warp w reads TMEM
+// lanes 32*(w%4)..+31 and owns 32 of the 128 output columns of the tile
+// (64 fp32 accumulators per thread, 96 registers per thread).
+#include "fbmoe_common.cuh"
+#include "fbmoe_launch.h"
+
+namespace fbmoe {
+namespace {
+
+constexpr int kThreads = 576;
+constexpr int kEpiWarps = 16;
+constexpr int kRows = 128;                       // token rows per block (== block_rows 128)
+constexpr int kTiles = kInter / 128;             // 16 tiles of 128 intermediate columns
+constexpr int kStages = 4;
+constexpr int kABytes = kRows * 128;             // 16 KB of gathered token rows
+constexpr int kBBytes = 256 * 128;               // 32 KB of W1 rows
+constexpr uint64_t kWaitBudgetNs = 4000000000ull;
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kABytes;
+constexpr int kOffBar = kOffB + kStages * kBBytes;
+constexpr int kNumBars = 2 * kStages + 4 + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory over the per-CTA limit");
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm1_rows_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_aperm,
+                      const float* __restrict__ a_scale_perm, const float* __restrict__ w1_scale,
+                      const int32_t* __restrict__ n_blocks_ptr, const int4* __restrict__ blocks,
+                      const int32_t* __restrict__ row_token, __half* __restrict__ inter,
+                      uint32_t* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = sm + kOffA;
+  uint8_t* sB = sm + kOffB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* tfull = bars + 2 * kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tfull + 4;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sm + kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);   // producer's expect_tx arrive (W1 tiles + row gathers)
+      mbar_init(&empty[s], 1);  // tcgen05.commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);  // one arrive per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *sAbort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w1);
+    tma_prefetch_desc(&tm_aperm);
+  }
+  if (warp == 1) {
+    tmem_alloc(sTmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *sTmem;
+  const int n_units = (*n_blocks_ptr) * kTiles;
+
+  auto fail = [&](uint32_t bit) {
+    *sAbort = 1;
+    atomicOr(status, bit);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    uint32_t issued_mask = 0, parity_mask = 0;  // per stage: ever issued / parity of the last issue
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const int4 blk = blocks[u / kTiles];
+      const int j = u % kTiles;
+      const int e = blk.x, r0 = blk.y;
+      const int wrow = e * kGemm1N + 128 * j;
+      for (int kb = 0; kb < kHBlocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutProducer);
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes);
+          tma_load_2d_nohint(sA + stage * kABytes, &tm_aperm, &full[stage], kb * kBlk, r0);
+          uint8_t* b = sB + stage * kBBytes;
+          tma_load_2d_nohint(b, &tm_w1, &full[stage], kb * kBlk, wrow);
+          tma_load_2d_nohint(b + 64 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + 64);
+          tma_load_2d_nohint(b + 128 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + kInter);
+          tma_load_2d_nohint(b + 192 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + kInter + 64);
+        }
+        issued_mask |= 1u << stage;
+        parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      // every issued load lands before the CTA exits
+      for (int s = 0; s < kStages; ++s)
+        if ((issued_mask >> s) & 1u)
+          if (!mbar_wait(&full[s], (parity_mask >> s) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+            fail(kStatusTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(0u, 128, 256);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t kbg = 0;
+      bool ok = true;
+      bool any = false;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        for (int kb = 0; kb < kHBlocks; ++kb) {
+          const uint32_t buf = kbg & 1u;
+          if (!mbar_wait(&tempty[buf], ((kbg >> 1) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
+              !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * kBBytes));
+          const uint32_t d = tmem_base + buf * 256;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_f8f6f4(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          tc_commit(&tfull[buf]);
+          any = true;
+          ++kbg;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (any) {
+        tc_commit(drain);
+        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;            // TMEM lane quarter
+    const int g = (warp - 2) >> 2;     // output columns [32g, 32g+32) of the tile
+    const int row = q * 32 + lane;     // token row in the block == TMEM lane
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint32_t kbg = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const int4 blk = blocks[u / kTiles];
+      const int j = u % kTiles;
+      const int e = blk.x, r0 = blk.y, nrows = blk.z;
+      const bool live = row < nrows;
+      const float* ws1 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + j) * kHBlocks;
+      const float* ws2 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + kIBlocks + j) * kHBlocks;
+      const float* asc = a_scale_perm + (size_t)(live ? r0 + row : 0) * kHBlocks;
+      float acc[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+      float a_next = live ? __ldg(asc) : 0.0f;
+      float s1_next = __ldg(ws1), s2_next = __ldg(ws2);
+      for (int kb = 0; kb < kHBlocks; ++kb) {
+        const float a_s = a_next, w_1 = s1_next, w_2 = s2_next;
+        if (kb + 1 < kHBlocks) {
+          a_next = live ? __ldg(asc + kb + 1) : 0.0f;
+          s1_next = __ldg(ws1 + kb + 1);
+          s2_next = __ldg(ws2 + kb + 1);
+        }
+        const uint32_t buf = kbg & 1u;
+        if (!mbar_wait(&tfull[buf], (kbg >> 1) & 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutEpilogue);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t0 = tmem_base + lane_base + buf * 256 + 32 * g;
+        const float f1 = a_s * w_1, f2 = a_s * w_2;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          // chunks 0-1: first-half columns (f1); 2-3: second half (f2)
+          float p[16];
+          tmem_ld16(t0 + (c < 2 ? 16 * c : 128 + 16 * (c - 2)), p);
+          tmem_wait_ld();
+          const float f = c < 2 ? f1 : f2;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(p[i], f, acc[16 * c + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        ++kbg;
+      }
+      if (!ok) break;
+      if (row < nrows) {
+        bool sat = false;
+        uint4* dst = reinterpret_cast<uint4*>(inter + (size_t)(r0 + row) * kInter + 128 * j + 32 * g);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const int c = 8 * v + 2 * h;
+            const float x2a = acc[32 + c], x2b = acc[32 + c + 1];
+            const float ya = x2a / (1.0f + expf(-x2a)) * acc[c];
+            const float yb = x2b / (1.0f + expf(-x2b)) * acc[c + 1];
+            const __half ha = to_half_sat(ya, sat), hb = to_half_sat(yb, sat);
+            w[h] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+          }
+          dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if (sat) atomicOr(status, kStatusSaturated);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const float* a_scale_perm,
+                              const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
+                              cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(gemm1_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (err != cudaSuccess) return err;
+    attr_set[dev] = true;
+  }
+  const long max_units = (long)L.max_blocks * kTiles;
+  int grid = (int)(max_units < num_sms ? max_units : num_sms);
+  if (grid < 1) grid = 1;
+  gemm1_rows_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
+      *tm_w1, *tm_aperm, a_scale_perm, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
+      reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const int32_t*>(ws + L.row_token),
+      reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
+  return cudaGetLastError();
+}
+
+}  // namespace fbmoe

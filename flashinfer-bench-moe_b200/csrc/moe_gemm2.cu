@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   using C = G2Cfg<BN>;
   constexpr int SR = C::kRawStages;
   constexpr int SC = C::kConvStages;
+  // Decode-sized blocks read each W2 tile about once: stream it past L2.
+  constexpr bool kStreamWeights = (BN <= 16);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sRaw = sm + C::kOffRaw;
@@ -168,8 +170,12 @@ __global__ void __launch_bounds__(kG2Threads, 1)
           }
           if (w2_side) {
             mbar_arrive_expect_tx(&fullb[ring.slot], C::kRawBytes);
-            tma_load_2d(sRaw + ring.slot * C::kRawBytes, &tm_w2, &fullb[ring.slot], kb * kBlk,
-                        e * kHidden + h * 128, pol);
+            if (kStreamWeights)
+              tma_load_2d(sRaw + ring.slot * C::kRawBytes, &tm_w2, &fullb[ring.slot], kb * kBlk,
+                          e * kHidden + h * 128, pol);
+            else
+              tma_load_2d_nohint(sRaw + ring.slot * C::kRawBytes, &tm_w2, &fullb[ring.slot], kb * kBlk,
+                                 e * kHidden + h * 128);
           } else {
             uint8_t* b = sB + ring.slot * C::kBBytes;
             mbar_arrive_expect_tx(&fullb[ring.slot], C::kBBytes);

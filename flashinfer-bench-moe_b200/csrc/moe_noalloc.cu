@@ -23,7 +23,7 @@
 // memory.
 #include <mutex>
 
-#include "../../include/fbmoe.h"
+#include "fbmoe.h"
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 

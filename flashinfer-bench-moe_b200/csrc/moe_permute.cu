@@ -8,8 +8,9 @@
 //  * each expert's row segment starts at a multiple of 16 rows, so every GEMM
 //    block of BN rows starts aligned, and the number of local experts is a
 //    runtime value (32, 64, 128 or 256 for expert-parallel shards).
-// The activations are NOT copied (reference main.py:1241-1271): GEMM1 gathers
-// token rows directly.
+// The activations are not copied here (reference main.py:1241-1271): for small
+// blocks GEMM1 gathers token rows itself; for 128-row blocks moe_gather.cu
+// copies them.  Padding rows get row_token = -1.
 //
 // One CTA of 1024 threads; tokens are processed in chunks of 1024.  Within a
 // chunk, a token's rank inside an expert is the number of set bits before it
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
         const int b = boff + j;
         if (b < max_blocks) blocks[b] = make_int4(e, off + j * bn, min(bn, c - j * bn), 0);
       }
+      for (int r = off + c; r < off + padded; ++r) row_token[r] = -1;  // padding rows
     }
     if (e == 0) {
       expert_poff[E_local] = tot_rows;

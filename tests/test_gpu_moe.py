@@ -73,6 +73,8 @@ CASES = [
     (901, "standard", 0, 12),
     (1024, "skew", 0, 12),
     (5000, "group", 0, 8),
+    (2500, "skew", 0, 12),
+    (4097, "standard", 0, 8),
     (4, "zero", 0, 4),
 ]
 
