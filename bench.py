@@ -56,46 +56,71 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed region.
 
-    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    NVML is polled from a background thread every 2 ms (timed regions can be a few
+    milliseconds long); if NVML is unavailable, nvidia-smi is sampled every 200 ms."""
+
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("hw_power_brake_slowdown", 0x80), ("sw_power_cap", 0x4))
 
     def __init__(self, device_index: int):
-        self.proc = None
         self.dev = device_index
+        self.samples = []
+        self.max_mhz = None
+        self.source = "none"
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                             int(get_reasons(h))))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.002)
+            self.source = "nvml"
+        except Exception:
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        out = subprocess.run(["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm",
+                                              "--format=csv,noheader,nounits", "-i", str(self.dev)],
+                                             capture_output=True, text=True, timeout=5).stdout
+                        mhz, mx = [float(x) for x in out.strip().split(",")[:2]]
+                        self.max_mhz = mx
+                        self.samples.append((mhz, 0))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.2)
+            self.source = "nvidia-smi"
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        self._stop.set()
+        self._thread.join(timeout=5)
         return False
 
     def summary(self):
-        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 6]
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        sm = [float(r[0]) for r in rows if r[0].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][1]) if rows[0][1].strip().replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0,
+                    "source": self.source}
+        mhz = [m for m, _ in self.samples]
+        reasons = sorted({name for _, bits in self.samples for name, bit in self.REASONS if bits & bit})
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": self.source}
 
 
 def dist_setup():
@@ -131,9 +156,9 @@ def max_over_ranks(x: float, world: int) -> float:
 
 # --------------------------------------------------------------------------- our arm
 def ep_inputs(world, rank):
+    import fbmoe_ep
     import fbmoe_workloads as W
-    E_local = E_TOTAL // world
-    off = rank * E_local
+    E_local, off = fbmoe_ep.shard(rank, world)
     weights = W.make_weights(E_local, 1000 + rank, "cuda")
     inp = W.make_inputs(T_EP, seed=0, config="standard", device="cuda", E_local=E_local,
                         local_expert_offset=off, weights=weights)
@@ -153,15 +178,14 @@ def make_step(inp, world, rank):
             L.forward(*args, off, scale, out=out, check=False)
             return out
         return step, out
-    import torch.distributed as dist
+    import fbmoe_ep
     partial = torch.empty((T, H), dtype=torch.float32, device="cuda")
     shard = torch.empty((T // world, H), dtype=torch.float32, device="cuda")
     out = torch.empty((T // world, H), dtype=torch.bfloat16, device="cuda")
 
     def step():
         L.forward(*args, off, scale, out=partial, check=False, partial_f32=True)
-        dist.reduce_scatter_tensor(shard, partial)
-        out.copy_(shard)
+        fbmoe_ep.combine(partial, out=out, scratch=shard)
         return out
     return step, out
 
@@ -252,9 +276,10 @@ def run_e2e(args, world, rank, inp, E_local, off):
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out_host.numel() * out_host.element_size()
     if world > 1:
-        import torch.distributed as dist
+        import fbmoe_ep
         partial = torch.empty((T_EP, H), dtype=torch.float32, device="cuda")
         shard = torch.empty((rows, H), dtype=torch.float32, device="cuda")
+        out_dev = torch.empty((rows, H), dtype=torch.bfloat16, device="cuda")
 
     def one():
         for k in names:
@@ -265,8 +290,7 @@ def run_e2e(args, world, rank, inp, E_local, off):
         else:
             L.forward(dev["routing_logits"], dev["routing_bias"], dev["hidden_states"], dev["hidden_states_scale"],
                       *w, off, inp["routed_scaling_factor"], out=partial, partial_f32=True)
-            dist.reduce_scatter_tensor(shard, partial)
-            o = shard.to(torch.bfloat16)
+            o = fbmoe_ep.combine(partial, out=out_dev, scratch=shard)
         out_host.copy_(o, non_blocking=True)
 
     n = max(3, min(args.steps, 10))

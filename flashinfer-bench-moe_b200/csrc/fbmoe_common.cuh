@@ -140,7 +140,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled bulk tensor load global -> shared (no multicast), completion on an mbarrier.
+// 2-D tiled bulk tensor load global -> this CTA's shared memory, completion on an mbarrier.
 // x = innermost coordinate (elements), y = row.  x * elem_size must be a multiple of 16.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                                             int32_t y, uint64_t cache_hint) {

@@ -1,0 +1,107 @@
+"""Expert-parallel host logic on CPU ranks (gloo, world size 2).
+
+The GPU path runs the same code over NCCL (bench.py --gpus N); here the
+shard assignment, the fp32 combine and the equivalence of sharded and
+unsharded computation are checked without a GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ATOL, ORACLE, PKG, RTOL
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shards_cover_all_experts_once():
+    import fbmoe_ep
+    for world in (1, 2, 4, 8):
+        owned = []
+        for r in range(world):
+            e_local, off = fbmoe_ep.shard(r, world)
+            assert e_local == 256 // world
+            owned.extend(range(off, off + e_local))
+        assert sorted(owned) == list(range(256))
+    with pytest.raises(ValueError):
+        fbmoe_ep.shard(0, 3)
+    with pytest.raises(ValueError):
+        fbmoe_ep.row_range(0, 3, 8)
+
+
+class LazyExperts:
+    """W1/W2 of global experts [offset, offset+n), generated per expert on demand."""
+
+    def __init__(self, offset, n, which, seed=5):
+        import fbmoe_workloads as W
+        self.W, self.offset, self.n, self.which, self.seed = W, offset, n, which, seed
+        self.shape = {"w1": (n, 4096, 7168), "s1": (n, 32, 56), "w2": (n, 7168, 2048), "s2": (n, 56, 16)}[which]
+
+    def __getitem__(self, le):
+        w1, s1, w2, s2 = self.W.make_weights(1, self.seed * 1000 + self.offset + le, "cpu")
+        return {"w1": w1, "s1": s1, "w2": w2, "s2": s2}[self.which][0]
+
+
+def _rank_main(rank, world, port, T, q):
+    import sys
+    for p in (PKG, ORACLE):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import fbmoe_ep
+        import fbmoe_workloads as W
+        import oracle
+        # (1) combine of random partials
+        g = torch.Generator().manual_seed(100 + rank)
+        part = torch.randn(T, 7168, generator=g)
+        mine = fbmoe_ep.combine(part.clone())
+        # (2) the operator on this rank's expert shard
+        e_local, off = fbmoe_ep.shard(rank, world)
+        logits, bias, hs, hs_scale = W.make_activations(T, seed=7, config="standard", device="cpu")
+        partial = oracle.run(logits, bias, hs, hs_scale, LazyExperts(off, e_local, "w1"),
+                             LazyExperts(off, e_local, "s1"), LazyExperts(off, e_local, "w2"),
+                             LazyExperts(off, e_local, "s2"), off, 2.5, return_fp32=True)
+        rows = fbmoe_ep.combine(partial)
+        q.put((rank, mine.view(torch.int16).numpy(), rows.view(torch.int16).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.slow
+def test_ep_combine_and_shard_equivalence_gloo(oracle_mod):
+    world, T = 2, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, T, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict()
+    for _ in range(world):
+        r, mine, rows = q.get(timeout=600)
+        got[r] = (torch.from_numpy(mine).view(torch.bfloat16), torch.from_numpy(rows).view(torch.bfloat16))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # (1) rank r holds rows [r*T/2, (r+1)*T/2) of the fp32 sum, rounded once
+    parts = [torch.randn(T, 7168, generator=torch.Generator().manual_seed(100 + r)) for r in range(world)]
+    total = (parts[0] + parts[1]).to(torch.bfloat16)
+    for r in range(world):
+        lo, hi = r * T // world, (r + 1) * T // world
+        assert torch.equal(got[r][0], total[lo:hi])
+    # (2) the combined shards equal the unsharded operator over all 256 experts
+    import fbmoe_workloads as W
+    logits, bias, hs, hs_scale = W.make_activations(T, seed=7, config="standard", device="cpu")
+    full = oracle_mod.run(logits, bias, hs, hs_scale, LazyExperts(0, 256, "w1"), LazyExperts(0, 256, "s1"),
+                          LazyExperts(0, 256, "w2"), LazyExperts(0, 256, "s2"), 0, 2.5)
+    combined = torch.cat([got[r][1] for r in range(world)])
+    st = oracle_mod.error_stats(combined, full, ATOL, RTOL)
+    assert st["frac_pass"] == 1.0 and st["max_abs"] <= 1e-2, st
