@@ -337,12 +337,17 @@ def decode_sweep(peaks):
         inp = W.make_inputs(T, seed=T, config="standard", device="cuda", weights=weights)
         args = W.as_args(inp)
         us = 1e3 * time_calls(lambda: L.forward(*args, check=False), 30, lambda: flush_l2(buf))
+        # stage breakdown from a separate pass: the events between stages serialise the launches
+        L.profile_begin(8)
+        time_calls(lambda: L.forward(*args, check=False), 5, lambda: flush_l2(buf))
+        stage_ms, nf = L.profile_end()
         pairs, active = local_pairs(inp, 32, 0)
         nbytes = active * BYTES_PER_EXPERT + BYTES_PER_TOKEN * T + 512
         gbs = nbytes / (us / 1e6) / 1e9
         res.append({"T": T, "us_per_call": round(us, 2), "active_experts": active, "local_pairs": pairs,
                     "algorithmic_bytes": nbytes, "hbm_gbs": round(gbs, 1),
-                    "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)})
+                    "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                    "stage_us_profiled": {n: round(1e3 * stage_ms[i] / max(nf, 1), 1) for i, n in enumerate(L.STAGES)}})
     del weights
     return {"config": "config1 decode, 32 local experts, offset 0, L2 flushed between calls",
             "peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"], "points": res}

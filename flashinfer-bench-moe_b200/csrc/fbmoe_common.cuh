@@ -60,6 +60,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// -------------------------------------------------- programmatic dependent launch
+// Kernels of the forward are launched with programmatic stream serialization:
+// a kernel may start while its predecessor is still running.  pdl_wait() blocks
+// the calling thread until the predecessor grid has completed and its writes are
+// visible; pdl_trigger() lets the successor grid be scheduled.  Every kernel
+// triggers only after its own wait, so anything a successor reads before its
+// wait comes from grids that have already completed.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// After pdl_wait, before TMA (async proxy) reads of what the predecessor wrote.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- smem ------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

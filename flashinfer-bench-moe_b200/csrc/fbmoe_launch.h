@@ -8,6 +8,23 @@
 
 namespace fbmoe {
 
+// Launch with programmatic stream serialization (see pdl_wait/pdl_trigger).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Offsets (bytes) of the sub-buffers inside the caller-provided workspace.
 struct Layout {
   size_t status;       // uint32[4]  device status word(s)
@@ -23,14 +40,24 @@ struct Layout {
   size_t inter;        // f16[pcap * 2048]   SwiGLU output, expert-contiguous rows
   size_t pair_out;     // f16[pcap * 7168]   weighted per-(token, expert) rows
   size_t a_perm;       // e4m3[pcap * 7168]  token rows in permuted order (128-row blocks only)
+  size_t splits;       // int32[2]: K splits of GEMM1 / GEMM2, chosen on the device per call
+  size_t split_count;  // int32[kSplitItems]: arrivals per GEMM1 unit (split-K fix-up)
+  size_t split_part;   // fp32[kSplitItems][128][16]: GEMM1 split partial sums
   size_t a_scale_perm; // fp32[pcap * 56]    their 1x128 scales, row-major (128-row blocks only)
   size_t total;        // bytes
   int pcap;            // row capacity (multiple of 128)
   int e_local;         // local experts the layout was made for
+  int pair_planes;     // planes of pair_out (GEMM2 K splits write separate planes)
+  int split_items;     // capacity of split_count / split_part (0: no split-K)
   int max_blocks;
 };
 
-Layout make_layout(int T, int E_local);
+// allow_split: reserve the split-K buffers used for 16-row (decode) blocks.
+Layout make_layout(int T, int E_local, bool allow_split = true);
+
+// Split-K of the decode GEMMs: at most kSplitItems (unit, split) partials.
+constexpr int kSplitItems = 1024;
+constexpr int kMaxPairPlanes = 4;
 int choose_block_rows(int T, int E_local);
 
 // Copies each routed token's row (and its 56 scales, row-major) to its permuted
@@ -43,8 +70,9 @@ cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, floa
                          float* topk_w, uint32_t* status, cudaStream_t stream);
 
 // Histogram / padded offsets / deterministic permutation / GEMM block list.
+// Also picks the K splits of the GEMMs for num_sms CTAs (see moe_permute.cu).
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
-                           int bn, const Layout& L, uint8_t* ws, cudaStream_t stream);
+                           int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream);
 
 // GEMM1 + SwiGLU: inter[row, :] for every local (token, expert) row.
 // tm_aperm: the permuted activation rows (a_perm) in 128-row boxes (used for block_rows 128).
@@ -76,6 +104,6 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
-                 size_t workspace_bytes, void* stream);
+                 size_t workspace_bytes, void* stream, bool allow_split = true);
 
 }  // namespace fbmoe

@@ -29,7 +29,7 @@ int choose_block_rows(int T, int E_local) {
   return 128;
 }
 
-Layout make_layout(int T, int E_local) {
+Layout make_layout(int T, int E_local, bool allow_split) {
   Layout L;
   const size_t tt = (size_t)(T > 0 ? T : 0);
   const int el = E_local > 0 ? E_local : 0;
@@ -55,8 +55,15 @@ Layout make_layout(int T, int E_local) {
   L.row_token = take((size_t)pcap * 4);
   L.row_weight = take((size_t)pcap * 4);
   L.inter = take((size_t)pcap * kInter * 2);
-  L.pair_out = take((size_t)pcap * kHidden * 2);
-  const bool big = choose_block_rows(T, E_local) == 128;
+  const int bn = choose_block_rows(T, E_local);
+  const bool split = allow_split && bn == 16;
+  L.pair_planes = split ? kMaxPairPlanes : 1;
+  L.split_items = split ? kSplitItems : 0;
+  L.pair_out = take((size_t)pcap * kHidden * 2 * L.pair_planes);
+  L.splits = take(16);
+  L.split_count = take((size_t)L.split_items * 4);
+  L.split_part = take((size_t)L.split_items * 128 * 16 * 4);
+  const bool big = bn == 128;
   L.a_perm = take(big ? (size_t)pcap * kHidden : 0);
   L.a_scale_perm = take(big ? (size_t)pcap * kHBlocks * 4 : 0);
   L.e_local = el;
@@ -165,10 +172,10 @@ int fbmoe_route(const float* routing_logits, const void* routing_bias, int T, fl
 
 namespace fbmoe {
 int forward_core(const float* routing_logits, const void* routing_bias, const void* hidden_states,
-                        const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
-                        const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
-                        int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out,
-                        void* workspace, size_t workspace_bytes, void* stream_) {
+                 const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                 const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
+                 int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
+                 size_t workspace_bytes, void* stream_, bool allow_split) {
   if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
   if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale || !gemm1_weights ||
@@ -177,7 +184,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
       !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(out, 16) || !aligned(workspace, 256))
     return FBMOE_ERR_MISALIGNED;
-  const Layout L = make_layout(T, E_local);
+  const Layout L = make_layout(T, E_local, allow_split);
   if (workspace_bytes < L.total) return FBMOE_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
@@ -215,7 +222,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                                reinterpret_cast<uint32_t*>(ws + L.status), stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 1, stream);
-  e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, L, ws, stream);
+  e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, sms, L, ws, stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 2, stream);
   if (bn == 128) {

@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(kWarps * 32) gather_rows_kernel(const uint8_t*
                                                                   uint8_t* __restrict__ a_perm,
                                                                   float* __restrict__ a_scale_perm) {
   const int lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   const int rows = *expert_poff_end;  // padded row count of all local experts
   for (int r = blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += gridDim.x * kWarps) {
     const int tok = row_token[r];
@@ -45,10 +47,10 @@ cudaError_t launch_gather_rows(const uint8_t* hidden, const float* hidden_scale,
   const int max_rows = L.pcap;
   int blocks = (max_rows + kWarps - 1) / kWarps;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  gather_rows_kernel<<<blocks, kWarps * 32, 0, stream>>>(
-      hidden, hidden_scale, T, reinterpret_cast<const int32_t*>(ws + L.expert_poff) + L.e_local,
-      reinterpret_cast<const int32_t*>(ws + L.row_token), ws + L.a_perm, reinterpret_cast<float*>(ws + L.a_scale_perm));
-  return cudaGetLastError();
+  return launch_pdl(gather_rows_kernel, dim3(blocks), dim3(kWarps * 32), 0, stream, hidden, hidden_scale, T,
+                    reinterpret_cast<const int32_t*>(ws + L.expert_poff) + L.e_local,
+                    reinterpret_cast<const int32_t*>(ws + L.row_token), ws + L.a_perm,
+                    reinterpret_cast<float*>(ws + L.a_scale_perm));
 }
 
 }  // namespace fbmoe

@@ -24,25 +24,45 @@
 // s1[e, n/128, kb] * a_scale[kb, t] and accumulate in fp32 registers (the
 // per-128-K promotion), so the fp32 block scales are applied exactly.
 //
-// Warp roles (256 threads): w0 producer (TMA + cp.async), w1 MMA issuer and
-// TMEM owner, w2-w3 idle, w4-w7 epilogue (TMEM lanes 0-127 = A rows).
+// Warp roles (128 + 128*G threads): w0 producer (TMA + cp.async), w1 MMA issuer
+// and TMEM owner, w2-w3 idle, then G sets of four epilogue warps (TMEM lanes
+// 0-127 = A rows).  Set j promotes the K-blocks kb = j (mod G) into its own
+// registers, with 2G TMEM buffers, so G K-blocks are in flight in the epilogue
+// and the per-K-block TMEM round trip does not bound the weight stream; the
+// sets' partial sums are added in fixed order (set 0 first) before SwiGLU.
+// G = 4 for 16-token blocks (decode), 2 for 32, 1 above.
+//
+// Split-K (16-token blocks): when few units exist (small T), the permute kernel
+// sets splits[0] = S > 1 and each unit's 56 K-blocks are shared by S work items
+// on different CTAs.  Every item writes its fp32 partial (128 rows x BN); the
+// item that arrives last on the unit's counter adds the S partials in split
+// order (deterministic), applies SwiGLU, writes the intermediate and clears
+// the counter for the next call.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
 namespace fbmoe {
 namespace {
 
-constexpr int kG1Threads = 256;
 constexpr int kG1Slices = kInter / 64;  // 32 slices of 64 output columns
-constexpr int kLag = 2;                 // cp.async completion lag (stages)
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;
 
 template <int BN>
 struct G1Cfg {
-  static constexpr int kStages = BN <= 16 ? 10 : BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
+  static constexpr int kSets = BN <= 16 ? 4 : BN <= 32 ? 2 : 1;   // epilogue warp sets
+  static constexpr int kThreads = 128 + 128 * kSets;
+  static constexpr int kBufs = 2 * kSets;                        // TMEM partial buffers
+  static constexpr int kStages = BN <= 16 ? 8 : BN <= 32 ? 7 : BN <= 64 ? 6 : 4;
+  // A stage's cp.async row copies are signalled complete kLag stages after they
+  // are issued (cp.async.wait_group kLag), so up to kLag stages of row copies
+  // are in flight; kLag <= kStages - 1 keeps the producer from waiting on its own
+  // unsignalled stages.
+  static constexpr int kLag = kStages - 2;
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = BN * 128;
-  static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  static constexpr int kTmemCols = (kBufs * BN < 32) ? 32 : kBufs * BN;
+  static_assert((kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols <= 512, "TMEM allocation must be a power of 2");
+  static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
   static constexpr int kXchStride = BN + 1;
   // layout (offsets from a 1024-aligned base)
   static constexpr int kOffA = 0;
@@ -50,20 +70,21 @@ struct G1Cfg {
   static constexpr int kOffAScale = kOffB + kStages * kBBytes;
   static constexpr int kOffWScale = kOffAScale + kHBlocks * BN * 4;
   static constexpr int kOffXch = kOffWScale + 2 * kHBlocks * 4;
-  static constexpr int kOffTok = kOffXch + 64 * kXchStride * 4;
+  static constexpr int kOffTok = kOffXch + kSets * 128 * kXchStride * 4;
   static constexpr int kOffBar = (kOffTok + BN * 4 + 7) / 8 * 8;
-  static constexpr int kNumBars = 2 * kStages + 4 + 1;
+  static constexpr int kNumBars = 2 * kStages + 2 * kBufs + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16 + 1024;  // + alignment slack
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kG1Threads, 1)
+__global__ void __launch_bounds__(G1Cfg<BN>::kThreads, 1)
     gemm1_swiglu_kernel(const __grid_constant__ CUtensorMap tm_w1, const uint8_t* __restrict__ hidden,
                         const float* __restrict__ hidden_scale, int T, const float* __restrict__ w1_scale,
                         const int32_t* __restrict__ n_blocks_ptr, const int4* __restrict__ blocks,
                         const int32_t* __restrict__ row_token, __half* __restrict__ inter,
-                        uint32_t* __restrict__ status) {
+                        uint32_t* __restrict__ status, const int32_t* __restrict__ splits,
+                        int32_t* __restrict__ split_count, float* __restrict__ split_part) {
   using C = G1Cfg<BN>;
   constexpr int S = C::kStages;
   // Decode-sized blocks read each weight tile about once: stream it past L2.
@@ -75,16 +96,17 @@ __global__ void __launch_bounds__(kG1Threads, 1)
   uint8_t* sB = sm + C::kOffB;
   float* sAScale = reinterpret_cast<float*>(sm + C::kOffAScale);  // [56][BN]
   float* sWScale = reinterpret_cast<float*>(sm + C::kOffWScale);  // [2][56]
-  float* sXch = reinterpret_cast<float*>(sm + C::kOffXch);        // [64][BN+1]
+  float* sXch = reinterpret_cast<float*>(sm + C::kOffXch);        // [sets][128][BN+1] partial sums
   int* sTok = reinterpret_cast<int*>(sm + C::kOffTok);            // [BN]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
-  uint64_t* tempty = bars + 2 * S + 2;
-  uint64_t* drain = bars + 2 * S + 4;
+  uint64_t* tempty = tfull + C::kBufs;
+  uint64_t* drain = tempty + C::kBufs;
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + C::kOffMisc);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sm + C::kOffMisc + 4);
+  volatile int* sLast = reinterpret_cast<volatile int*>(sm + C::kOffMisc + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -94,9 +116,9 @@ __global__ void __launch_bounds__(kG1Threads, 1)
       mbar_init(&full[s], 2);   // producer expect_tx arrive + cp.async completion arrive
       mbar_init(&empty[s], 1);  // tcgen05.commit
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kBufs; ++b) {
       mbar_init(&tfull[b], 1);   // tcgen05.commit
-      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[b], 4);  // one arrive per warp of the set that owns the K-block
     }
     mbar_init(drain, 1);
     *sAbort = 0;
@@ -110,9 +132,15 @@ __global__ void __launch_bounds__(kG1Threads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
+  fence_proxy_async_global();
   const uint32_t tmem_base = *sTmem;
 
   const int n_units = (*n_blocks_ptr) * kG1Slices;
+  const int n_split = splits[0];                 // K splits per unit (1 unless decode)
+  const int nk = kHBlocks / n_split;             // K-blocks per work item
+  const int n_items = n_units * n_split;
 
   auto fail = [&](uint32_t bit) {
     *sAbort = 1;
@@ -129,7 +157,8 @@ __global__ void __launch_bounds__(kG1Threads, 1)
     uint32_t last_parity[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) last_parity[s] = 0xFFFFFFFFu;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int u = it / n_split, sp = it % n_split;
       const int4 blk = blocks[u / kG1Slices];
       const int g = u % kG1Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
@@ -143,7 +172,7 @@ __global__ void __launch_bounds__(kG1Threads, 1)
       }
       const int wrow1 = e * kGemm1N + 64 * g;
       const int wrow2 = wrow1 + kInter;
-      for (int kb = 0; kb < kHBlocks; ++kb) {
+      for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutProducer);
@@ -168,11 +197,11 @@ __global__ void __launch_bounds__(kG1Threads, 1)
         }
         cp_async_commit();
         ++issued;
-        if (issued > kLag) {
-          cp_async_wait_group<kLag>();
+        if (issued > C::kLag) {
+          cp_async_wait_group<C::kLag>();
           fence_proxy_async_smem();
           __syncwarp();
-          int ps = stage - kLag;
+          int ps = stage - C::kLag;
           if (ps < 0) ps += S;
           if (lane == 0) mbar_arrive(&full[ps]);
         }
@@ -187,7 +216,7 @@ __global__ void __launch_bounds__(kG1Threads, 1)
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      const long tail = issued < kLag ? issued : kLag;
+      const long tail = issued < C::kLag ? issued : C::kLag;
       for (long i = tail; i >= 1; --i) {
         int ps = stage - (int)i;
         while (ps < 0) ps += S;
@@ -209,10 +238,10 @@ __global__ void __launch_bounds__(kG1Threads, 1)
       uint32_t kbg = 0;
       bool ok = true;
       bool any = false;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        for (int kb = 0; kb < kHBlocks; ++kb) {
-          const uint32_t buf = kbg & 1u;
-          if (!mbar_wait(&tempty[buf], ((kbg >> 1) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        for (int l = 0; l < nk; ++l) {
+          const uint32_t buf = kbg % C::kBufs;
+          if (!mbar_wait(&tempty[buf], ((kbg / C::kBufs) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
               !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
@@ -243,13 +272,17 @@ __global__ void __launch_bounds__(kG1Threads, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 4;           // TMEM lane quarter
+    constexpr int G = C::kSets;
+    constexpr uint32_t kEpiThreads = 128 * G;
+    const int set = (warp - 4) >> 2;   // this warp's K-block residue class
+    const int ew = warp & 3;           // TMEM lane quarter
     const int row = ew * 32 + lane;    // A row == TMEM lane
     const int etid = threadIdx.x - 128;
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    uint32_t kbg = 0;
+    uint32_t kbg = 0;                  // K-blocks this CTA processed before the current item
     bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int u = it / n_split, sp = it % n_split;
       const int4 blk = blocks[u / kG1Slices];
       const int g = u % kG1Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
@@ -259,27 +292,30 @@ __global__ void __launch_bounds__(kG1Threads, 1)
         const int nb = h * (kInter / kBlk) + g / 2;
         sWScale[etid] = w1_scale[((size_t)e * (kGemm1N / kBlk) + nb) * kHBlocks + kb];
       }
-      named_barrier_sync(1, 128);
-      for (int i = etid; i < kHBlocks * BN; i += 128) {
+      named_barrier_sync(1, kEpiThreads);
+      for (int i = etid; i < kHBlocks * BN; i += kEpiThreads) {
         const int kb = i / BN, t = i % BN;
         const int tok = sTok[t];
         sAScale[i] = tok >= 0 ? hidden_scale[(size_t)kb * T + tok] : 0.0f;
       }
-      named_barrier_sync(1, 128);
+      named_barrier_sync(1, kEpiThreads);
 
       float acc[BN];
 #pragma unroll
       for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
       const float* wsc = sWScale + (ew < 2 ? 0 : kHBlocks);
       bool bad = false;
-      for (int kb = 0; kb < kHBlocks; ++kb) {
-        const uint32_t buf = kbg & 1u;
-        if (!mbar_wait(&tfull[buf], (kbg >> 1) & 1u, sAbort, kWaitBudgetNs)) {
+      // this set takes the item's K-blocks whose CTA-wide index is = set (mod G)
+      for (int l = (set - (int)(kbg % G) + G) % G; l < nk; l += G) {
+        const uint32_t kgl = kbg + l;
+        const uint32_t buf = kgl % C::kBufs;
+        if (!mbar_wait(&tfull[buf], (kgl / C::kBufs) & 1u, sAbort, kWaitBudgetNs)) {
           bad = true;
           if (lane == 0) fail(kStatusTimeoutEpilogue);
           break;
         }
         tc_fence_after();
+        const int kb = sp * nk + l;
         const float ws = wsc[kb];
         const float* asc = sAScale + kb * BN;
 #pragma unroll
@@ -293,31 +329,64 @@ __global__ void __launch_bounds__(kG1Threads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
-        ++kbg;
       }
-      // SwiGLU: rows 64..127 (silu half) hand their values to rows 0..63.
-      if (ew >= 2 && !bad) {
+      kbg += nk;
+      // Each set publishes its partial sums; they are added in set order.
+      if (!bad) {
+        float* mine = sXch + (size_t)(set * 128 + row) * C::kXchStride;
 #pragma unroll
-        for (int t = 0; t < BN; ++t) sXch[(row - 64) * C::kXchStride + t] = acc[t];
+        for (int t = 0; t < BN; ++t) mine[t] = acc[t];
       }
-      if (named_barrier_or(1, 128, bad)) {
+      if (named_barrier_or(1, kEpiThreads, bad)) {
         ok = false;
         break;
       }
-      if (ew < 2) {
-        __half* dst = inter + (size_t)r0 * kInter + 64 * g + row;
-        bool sat = false;
+      bool last = true;
+      if (n_split > 1) {
+        // publish this item's partial, then find out whether it completes the unit
+        float* part = split_part + (size_t)it * 128 * BN;
+        for (int i = etid; i < 128 * BN; i += kEpiThreads) {
+          const int r = i / BN, t = i % BN;
+          float v = 0.0f;
 #pragma unroll
-        for (int t = 0; t < BN; ++t) {
+          for (int j = 0; j < G; ++j) v += sXch[(size_t)(j * 128 + r) * C::kXchStride + t];
+          part[i] = v;
+        }
+        __threadfence();
+        named_barrier_sync(1, kEpiThreads);
+        if (etid == 0) *sLast = (atomicAdd(&split_count[u], 1) == n_split - 1) ? 1 : 0;
+        named_barrier_sync(1, kEpiThreads);
+        last = *sLast != 0;
+        if (last) __threadfence();
+      }
+      if (last) {
+        // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).
+        const float* parts = split_part + (size_t)u * n_split * 128 * BN;
+        for (int i = etid; i < 64 * BN; i += kEpiThreads) {
+          const int r = i % 64, t = i / 64;
           if (t < nrows) {
-            const float x2 = sXch[row * C::kXchStride + t];
+            float x1 = 0.0f, x2 = 0.0f;
+            if (n_split == 1) {
+#pragma unroll
+              for (int j = 0; j < G; ++j) {
+                x1 += sXch[(size_t)(j * 128 + r) * C::kXchStride + t];
+                x2 += sXch[(size_t)(j * 128 + 64 + r) * C::kXchStride + t];
+              }
+            } else {
+              for (int q = 0; q < n_split; ++q) {
+                x1 += __ldcg(parts + (size_t)q * 128 * BN + r * BN + t);
+                x2 += __ldcg(parts + (size_t)q * 128 * BN + (64 + r) * BN + t);
+              }
+            }
+            bool sat = false;
             const float silu = x2 / (1.0f + expf(-x2));
-            dst[(size_t)t * kInter] = to_half_sat(silu * acc[t], sat);
+            inter[(size_t)(r0 + t) * kInter + 64 * g + r] = to_half_sat(silu * x1, sat);
+            if (sat) atomicOr(status, kStatusSaturated);
           }
         }
-        if (sat) atomicOr(status, kStatusSaturated);
+        if (n_split > 1 && etid == 0) split_count[u] = 0;  // ready for the next call
       }
-      named_barrier_sync(1, 128);
+      named_barrier_sync(1, kEpiThreads);
     }
   }
 
@@ -346,11 +415,12 @@ cudaError_t launch_g1(const CUtensorMap* tm, const uint8_t* hidden, const float*
   long max_units = (long)L.max_blocks * kG1Slices;
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;
-  gemm1_swiglu_kernel<BN><<<grid, kG1Threads, C::kBytes, stream>>>(
-      *tm, hidden, hidden_scale, T, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
-      reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const int32_t*>(ws + L.row_token),
-      reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
-  return cudaGetLastError();
+  return launch_pdl(gemm1_swiglu_kernel<BN>, dim3(grid), dim3(C::kThreads), C::kBytes, stream, *tm, hidden,
+                    hidden_scale, T, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
+                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const int32_t*>(ws + L.row_token),
+                    reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status),
+                    reinterpret_cast<const int32_t*>(ws + L.splits), reinterpret_cast<int32_t*>(ws + L.split_count),
+                    reinterpret_cast<float*>(ws + L.split_part));
 }
 
 }  // namespace

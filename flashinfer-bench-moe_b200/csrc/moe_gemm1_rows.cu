@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
+  fence_proxy_async_global();
   const uint32_t tmem_base = *sTmem;
   const int n_units = (*n_blocks_ptr) * kTiles;
 
@@ -198,19 +201,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool live = row < nrows;
       const float* ws1 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + j) * kHBlocks;
       const float* ws2 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + kIBlocks + j) * kHBlocks;
-      const float* asc = a_scale_perm + (size_t)(live ? r0 + row : 0) * kHBlocks;
+      // Row scales: 56 contiguous floats, read 4 K-blocks at a time, one group
+      // ahead.  W1 scales: lane l holds K-blocks l and 32+l, picked by shuffle.
+      const float4* asc4 = reinterpret_cast<const float4*>(a_scale_perm + (size_t)(live ? r0 + row : 0) * kHBlocks);
+      const float w1a = __ldg(ws1 + lane), w1b = lane < kHBlocks - 32 ? __ldg(ws1 + 32 + lane) : 0.0f;
+      const float w2a = __ldg(ws2 + lane), w2b = lane < kHBlocks - 32 ? __ldg(ws2 + 32 + lane) : 0.0f;
       float acc[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
-      float a_next = live ? __ldg(asc) : 0.0f;
-      float s1_next = __ldg(ws1), s2_next = __ldg(ws2);
+      float4 a_cur = __ldg(asc4), a_nxt = __ldg(asc4 + 1);
       for (int kb = 0; kb < kHBlocks; ++kb) {
-        const float a_s = a_next, w_1 = s1_next, w_2 = s2_next;
-        if (kb + 1 < kHBlocks) {
-          a_next = live ? __ldg(asc + kb + 1) : 0.0f;
-          s1_next = __ldg(ws1 + kb + 1);
-          s2_next = __ldg(ws2 + kb + 1);
+        if ((kb & 3) == 0 && kb > 0) {
+          a_cur = a_nxt;
+          if (kb + 4 < kHBlocks) a_nxt = __ldg(asc4 + (kb >> 2) + 1);
         }
+        const float a_pick = (kb & 3) == 0 ? a_cur.x : (kb & 3) == 1 ? a_cur.y : (kb & 3) == 2 ? a_cur.z : a_cur.w;
+        const float a_s = live ? a_pick : 0.0f;
+        const float w_1 = __shfl_sync(0xffffffffu, kb < 32 ? w1a : w1b, kb & 31);
+        const float w_2 = __shfl_sync(0xffffffffu, kb < 32 ? w2a : w2b, kb & 31);
         const uint32_t buf = kbg & 1u;
         if (!mbar_wait(&tfull[buf], (kbg >> 1) & 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
@@ -282,11 +290,10 @@ cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_ap
   const long max_units = (long)L.max_blocks * kTiles;
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;
-  gemm1_rows_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      *tm_w1, *tm_aperm, a_scale_perm, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
-      reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const int32_t*>(ws + L.row_token),
-      reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
-  return cudaGetLastError();
+  return launch_pdl(gemm1_rows_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, *tm_w1, *tm_aperm,
+                    a_scale_perm, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
+                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const int32_t*>(ws + L.row_token),
+                    reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
 }
 
 }  // namespace fbmoe

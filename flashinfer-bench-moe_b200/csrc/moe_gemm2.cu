@@ -19,9 +19,15 @@
 // columns); its accumulator is double-buffered in TMEM so the epilogue of one
 // unit overlaps the MMAs of the next.
 //
-// Two shared-memory rings: a deep ring of raw FP8 W2 tiles (16 KB each; the
-// bytes that stream from HBM) and a 2-deep ring of converted f16 W2 tiles plus
-// the intermediate rows the MMA reads.
+// Split-K (decode): with splits[1] = S > 1 each unit's 16 K-blocks are shared
+// by S work items; item s writes plane s of pair_out and the combine kernel adds
+// the planes.
+//
+// Three shared-memory rings: a ring of raw FP8 W2 tiles (16 KB each; the bytes
+// that stream from HBM), a ring of converted f16 W2 tiles (3 deep for small
+// blocks, so the converters run two stages ahead of the MMA), and a
+// deep ring of intermediate rows (their L2 latency must not sit on the critical
+// path: with the rows in the converted ring, decode ran at ~10 GB/s per SM).
 //
 // Warp roles (384 threads): w0 W2 producer (TMA), w1 MMA issuer + TMEM owner,
 // w2 intermediate producer (TMA), w3 idle, w4-w7 converters (one W2 row each),
@@ -38,8 +44,9 @@ constexpr uint64_t kWaitBudgetNs = 4000000000ull;
 
 template <int BN>
 struct G2Cfg {
-  static constexpr int kRawStages = BN <= 16 ? 8 : BN <= 32 ? 7 : BN <= 64 ? 6 : 4;
-  static constexpr int kConvStages = 2;
+  static constexpr int kRawStages = BN <= 32 ? 4 : 3;
+  static constexpr int kConvStages = BN <= 32 ? 3 : 2;
+  static constexpr int kBStages = BN <= 16 ? 6 : BN <= 32 ? 4 : BN <= 64 ? 4 : 2;
   static constexpr int kRawBytes = 128 * 128;      // fp8 W2 tile
   static constexpr int kAhBytes = 2 * 128 * 128;   // f16 W2 tile (two 64-K halves)
   static constexpr int kBBytes = BN * 256;         // f16 intermediate rows (two 64-K halves)
@@ -47,8 +54,8 @@ struct G2Cfg {
   static constexpr int kOffRaw = 0;
   static constexpr int kOffAh = kOffRaw + kRawStages * kRawBytes;
   static constexpr int kOffB = kOffAh + kConvStages * kAhBytes;
-  static constexpr int kOffBar = kOffB + kConvStages * kBBytes;
-  static constexpr int kNumBars = 2 * kRawStages + 3 * kConvStages + 4 + 1;
+  static constexpr int kOffBar = kOffB + kBStages * kBBytes;
+  static constexpr int kNumBars = 2 * kRawStages + 2 * kConvStages + 2 * kBStages + 4 + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16 + 1024;
 };
@@ -83,10 +90,12 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     gemm2_combine_kernel(const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_inter,
                          const float* __restrict__ w2_scale, const int32_t* __restrict__ n_blocks_ptr,
                          const int4* __restrict__ blocks, const float* __restrict__ row_weight,
-                         __half* __restrict__ pair_out, uint32_t* __restrict__ status) {
+                         __half* __restrict__ pair_out, uint32_t* __restrict__ status,
+                         const int32_t* __restrict__ splits, size_t plane_elems) {
   using C = G2Cfg<BN>;
   constexpr int SR = C::kRawStages;
   constexpr int SC = C::kConvStages;
+  constexpr int SB = C::kBStages;
   // Decode-sized blocks read each W2 tile about once: stream it past L2.
   constexpr bool kStreamWeights = (BN <= 16);
   extern __shared__ uint8_t smem_raw[];
@@ -97,10 +106,11 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
   uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
   uint64_t* raw_empty = bars + SR;             // converters done reading it
-  uint64_t* b_full = bars + 2 * SR;            // intermediate rows landed (TMA)
-  uint64_t* a_full = bars + 2 * SR + SC;       // f16 W2 tile written by the converters
-  uint64_t* c_empty = bars + 2 * SR + 2 * SC;  // MMA done with the converted slot
-  uint64_t* tfull = bars + 2 * SR + 3 * SC;
+  uint64_t* a_full = bars + 2 * SR;            // f16 W2 tile written by the converters
+  uint64_t* c_empty = bars + 2 * SR + SC;       // MMA done with the converted slot
+  uint64_t* b_full = bars + 2 * SR + 2 * SC;    // intermediate rows landed (TMA)
+  uint64_t* b_empty = b_full + SB;              // MMA done with the intermediate slot
+  uint64_t* tfull = b_empty + SB;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tfull + 4;
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + C::kOffMisc);
@@ -115,9 +125,12 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       mbar_init(&raw_empty[s], 4);
     }
     for (int s = 0; s < SC; ++s) {
-      mbar_init(&b_full[s], 1);
       mbar_init(&a_full[s], 4);
       mbar_init(&c_empty[s], 1);
+    }
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -138,8 +151,15 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The block list and row weights come from the permute kernel, which finished
+  // before GEMM1 let this grid launch; only the intermediate rows (GEMM1's
+  // output) need the wait, done by the thread that loads them.
+  pdl_trigger();
   const uint32_t tmem_base = *sTmem;
   const int n_units = (*n_blocks_ptr) * kG2Slices;
+  const int n_split = splits[1];                  // K splits per unit (1 unless decode)
+  const int nk = kIBlocks / n_split;              // K-blocks per work item
+  const int n_items = n_units * n_split;
 
   auto fail = [&](uint32_t bit) {
     *sAbort = 1;
@@ -150,19 +170,24 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     // ------------------------------------------------------------ producers
     if (lane == 0) {
       const bool w2_side = (warp == 0);
+      if (!w2_side) {
+        pdl_wait();
+        fence_proxy_async_global();
+      }
       const uint64_t pol = w2_side ? l2_policy_evict_first() : l2_policy_evict_last();
-      const int n = w2_side ? SR : SC;
+      const int n = w2_side ? SR : SB;
       uint64_t* fullb = w2_side ? raw_full : b_full;
-      uint64_t* emptyb = w2_side ? raw_empty : c_empty;
+      uint64_t* emptyb = w2_side ? raw_empty : b_empty;
       Ring ring(n);
       bool ok = true;
-      uint32_t last_parity[SR > SC ? SR : SC];
+      uint32_t last_parity[SR > SB ? SR : SB];
       for (int s = 0; s < n; ++s) last_parity[s] = 0xFFFFFFFFu;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const int u = it / n_split, sp = it % n_split;
         const int4 blk = blocks[u / kG2Slices];
         const int h = u % kG2Slices;
         const int e = blk.x, r0 = blk.y;
-        for (int kb = 0; kb < kIBlocks; ++kb) {
+        for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
           if (!mbar_wait(&emptyb[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutProducer);
@@ -196,11 +221,11 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, BN);  // f16 x f16
-      Ring ring(SC);
+      Ring ring(SC), bring(SB);
       uint32_t ug = 0;
       bool ok = true;
       bool any = false;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ug) {
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ug) {
         const uint32_t buf = ug & 1u;
         if (!mbar_wait(&tempty[buf], ((ug >> 1) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
@@ -209,9 +234,9 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
-        for (int kb = 0; kb < kIBlocks; ++kb) {
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs) ||
-              !mbar_wait(&b_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
+              !mbar_wait(&b_full[bring.slot], bring.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
@@ -220,14 +245,16 @@ __global__ void __launch_bounds__(kG2Threads, 1)
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             const uint64_t adesc = umma_desc_sw128(smem_u32(sAh + ring.slot * C::kAhBytes + half * 128 * 128));
-            const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + ring.slot * C::kBBytes + half * BN * 128));
+            const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + bring.slot * C::kBBytes + half * BN * 128));
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               mma_f16(d, adesc + 2 * j, bdesc + 2 * j, idesc, (kb | half | j) ? 1u : 0u);
           }
           tc_commit(&c_empty[ring.slot]);
+          tc_commit(&b_empty[bring.slot]);
           any = true;
           ring.next();
+          bring.next();
         }
         if (!ok) break;
         tc_commit(&tfull[buf]);
@@ -243,18 +270,21 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     const int r = threadIdx.x - 128;  // W2 row within the tile
     Ring rr(SR), cr(SC);
     bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int u = it / n_split, sp = it % n_split;
       const int4 blk = blocks[u / kG2Slices];
       const int h = u % kG2Slices;
       const float* sc = w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
-      for (int kb = 0; kb < kIBlocks; ++kb) {
+      // the unit's 16 scales, one per lane: no global load on the per-stage path
+      const float lane_scale = __ldg(sc + (lane & (kIBlocks - 1)));
+      for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
         if (!mbar_wait(&raw_full[rr.slot], rr.phase, sAbort, kWaitBudgetNs) ||
             !mbar_wait(&c_empty[cr.slot], cr.phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutConvert);
           break;
         }
-        const float scale = __ldg(sc + kb);
+        const float scale = __shfl_sync(0xffffffffu, lane_scale, kb);
         const uint8_t* raw = sRaw + rr.slot * C::kRawBytes;
         uint8_t* ah = sAh + cr.slot * C::kAhBytes;
 #pragma unroll
@@ -286,7 +316,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
     uint32_t ug = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ug) {
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ug) {
+      const int u = it / n_split, sp = it % n_split;
       const int4 blk = blocks[u / kG2Slices];
       const int h = u % kG2Slices;
       const int r0 = blk.y, nrows = blk.z;
@@ -297,7 +328,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         break;
       }
       tc_fence_after();
-      __half* dst = pair_out + (size_t)r0 * kHidden + h * 128 + hrow;
+      __half* dst = pair_out + (size_t)sp * plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
       const float* wrow = row_weight + r0;
       bool sat = false;
 #pragma unroll
@@ -343,11 +374,11 @@ cudaError_t launch_g2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, con
   long max_units = (long)L.max_blocks * kG2Slices;
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;
-  gemm2_combine_kernel<BN><<<grid, kG2Threads, C::kBytes, stream>>>(
-      *tm_w2, *tm_inter, w2_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
-      reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const float*>(ws + L.row_weight),
-      reinterpret_cast<__half*>(ws + L.pair_out), reinterpret_cast<uint32_t*>(ws + L.status));
-  return cudaGetLastError();
+  return launch_pdl(gemm2_combine_kernel<BN>, dim3(grid), dim3(kG2Threads), C::kBytes, stream, *tm_w2, *tm_inter,
+                    w2_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
+                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const float*>(ws + L.row_weight),
+                    reinterpret_cast<__half*>(ws + L.pair_out), reinterpret_cast<uint32_t*>(ws + L.status),
+                    reinterpret_cast<const int32_t*>(ws + L.splits), (size_t)L.pcap * kHidden);
 }
 
 }  // namespace

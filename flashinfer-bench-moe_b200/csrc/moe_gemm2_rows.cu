@@ -128,6 +128,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The block list and row weights come from the permute kernel, which finished
+  // before GEMM1 let this grid launch; only the intermediate rows (GEMM1's
+  // output) need the wait, done by the thread that loads them.
+  pdl_trigger();
   const uint32_t tmem_base = *sTmem;
   const int n_units = (*n_blocks_ptr) * kNTiles;
 
@@ -140,6 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producers
     if (lane == 0) {
       const bool w2_side = (warp == 0);
+      if (!w2_side) {
+        pdl_wait();
+        fence_proxy_async_global();
+      }
       const int n = w2_side ? kRawStages : kConvStages;
       uint64_t* fullb = w2_side ? raw_full : a_full;
       uint64_t* emptyb = w2_side ? raw_empty : c_empty;
@@ -226,6 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* s_lo = w2_scale + ((size_t)blk.x * kHBlocks + 2 * nt) * kIBlocks;  // rows 0..127
       const float* s_hi = s_lo + kIBlocks;                                           // rows 128..255
       const int k_lo = block_exponent(s_lo), k_hi = block_exponent(s_hi);
+      // lanes 0-15 hold the first block's 16 scales, lanes 16-31 the second's
+      const float lane_scale = __ldg((lane < 16 ? s_lo : s_hi) + (lane & 15));
       for (int ks = 0; ks < kKSteps; ++ks) {
         if (!mbar_wait(&raw_full[rr.slot], rr.phase, sAbort, kWaitBudgetNs) ||
             !mbar_wait(&c_empty[cr.slot], cr.phase ^ 1u, sAbort, kWaitBudgetNs)) {
@@ -233,8 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) fail(kStatusTimeoutConvert);
           break;
         }
-        const __half h_lo = __float2half_rn(ldexpf(__ldg(s_lo + ks / 2), k_lo));
-        const __half h_hi = __float2half_rn(ldexpf(__ldg(s_hi + ks / 2), k_hi));
+        const __half h_lo = __float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, ks / 2), k_lo));
+        const __half h_hi = __float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, 16 + ks / 2), k_hi));
         const uint8_t* raw = sRaw + rr.slot * kRawBytes;
         uint8_t* wt = sW + cr.slot * kWBytes;
 #pragma unroll
@@ -338,11 +348,10 @@ cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm
   const long max_units = (long)L.max_blocks * kNTiles;
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;
-  gemm2_rows_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      *tm_w2raw, *tm_inter, w2_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
-      reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const float*>(ws + L.row_weight),
-      reinterpret_cast<__half*>(ws + L.pair_out), reinterpret_cast<uint32_t*>(ws + L.status));
-  return cudaGetLastError();
+  return launch_pdl(gemm2_rows_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, *tm_w2raw, *tm_inter, w2_scale,
+                    reinterpret_cast<const int32_t*>(ws + L.n_blocks), reinterpret_cast<const int4*>(ws + L.blocks),
+                    reinterpret_cast<const float*>(ws + L.row_weight), reinterpret_cast<__half*>(ws + L.pair_out),
+                    reinterpret_cast<uint32_t*>(ws + L.status));
 }
 
 }  // namespace fbmoe

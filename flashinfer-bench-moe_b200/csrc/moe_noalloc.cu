@@ -48,7 +48,7 @@ int scratch_for_current_device(void** out) {
   if (dev < 0 || dev >= kMaxDevices) return FBMOE_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lk(g_setup_mu);
   if (g_scratch_ptr[dev] == nullptr) {
-    if (make_layout(kNoAllocMaxTokens, kNoAllocMaxExperts).total > kNoAllocScratchBytes)
+    if (make_layout(kNoAllocMaxTokens, kNoAllocMaxExperts, false).total > kNoAllocScratchBytes)
       return FBMOE_ERR_NOALLOC_LIMIT;
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
@@ -76,5 +76,6 @@ extern "C" int fbmoe_forward_noalloc(const float* routing_logits, const void* ro
   if (rc != FBMOE_OK) return rc;
   return forward_core(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
-                      routed_scaling_factor, out, false, scratch, kNoAllocScratchBytes, stream);
+                      routed_scaling_factor, out, false, scratch, kNoAllocScratchBytes, stream,
+                      /*allow_split=*/false);
 }

@@ -12,6 +12,9 @@
 // blocks GEMM1 gathers token rows itself; for 128-row blocks moe_gather.cu
 // copies them.  Padding rows get row_token = -1.
 //
+// It also chooses the K splits of the decode GEMMs for this call from the block
+// count (see pick_split) and clears the split-K arrival counters.
+//
 // One CTA of 1024 threads; tokens are processed in chunks of 1024.  Within a
 // chunk, a token's rank inside an expert is the number of set bits before it
 // in that expert's 1024-bit membership mask, which is order-independent.
@@ -34,7 +37,30 @@ struct PermuteSmem {
   uint32_t bits[kMaxLocal][kWordsPerChunk];
   uint16_t wpre[kMaxLocal][kWordsPerChunk];
   int scan_tmp[2][kMaxLocal / 32];
+  int n_blocks;
+  int split1;
 };
+
+// Smallest split S of `units` work units (from `cand`, ascending) whose S*units
+// items fill `sms` CTAs to >= 85% of their last wave; otherwise the best one.
+// Splits cost a partial write/read per item, hence the preference for small S.
+__device__ int pick_split(int units, int sms, const int* cand, int ncand, int max_items) {
+  int best = 1;
+  float best_eff = -1.0f;
+  for (int i = 0; i < ncand; ++i) {
+    const int S = cand[i];
+    const long items = (long)units * S;
+    if (S > 1 && items > max_items) break;
+    const float waves = (float)items / (float)sms;
+    const float eff = waves / ceilf(waves);
+    if (eff >= 0.85f) return S;
+    if (eff > best_eff + 0.02f) {
+      best_eff = eff;
+      best = S;
+    }
+  }
+  return best;
+}
 
 // Exclusive scan of one value per thread over threads 0..255 (8 warps).
 __device__ __forceinline__ int block_excl_scan_256(int v, int* tmp, int* total) {
@@ -66,12 +92,17 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
                                                           int max_blocks, int32_t* __restrict__ row_token,
                                                           float* __restrict__ row_weight,
                                                           int32_t* __restrict__ token_rows,
-                                                          uint32_t* __restrict__ status) {
+                                                          uint32_t* __restrict__ status, int num_sms,
+                                                          int32_t* __restrict__ splits,
+                                                          int32_t* __restrict__ split_count, int split_items,
+                                                          int pair_planes) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   PermuteSmem& S = *reinterpret_cast<PermuteSmem*>(smem_raw);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
 
+  pdl_wait();
+  pdl_trigger();
   for (int e = tid; e < kMaxLocal; e += kThreads) S.count[e] = 0;
   __syncthreads();
 
@@ -107,11 +138,28 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
     }
     if (e == 0) {
       expert_poff[E_local] = tot_rows;
-      *n_blocks = min(tot_blocks, max_blocks);
+      const int nb_all = min(tot_blocks, max_blocks);
+      *n_blocks = nb_all;
       if (tot_blocks > max_blocks) atomicOr(status, kStatusBadTile);
+      int s1 = 1, s2 = 1;
+      if (split_items > 0 && nb_all > 0) {
+        const int c1[5] = {1, 2, 4, 7, 8};  // divisors of the 56 K-blocks of GEMM1
+        const int c2[3] = {1, 2, 4};        // divisors of the 16 K-blocks of GEMM2
+        s1 = pick_split(nb_all * (kInter / 64), num_sms, c1, 5, split_items);
+        s2 = pick_split(nb_all * (kHidden / 128), num_sms, c2, pair_planes >= 4 ? 3 : pair_planes >= 2 ? 2 : 1,
+                        1 << 30);
+      }
+      splits[0] = s1;
+      splits[1] = s2;
+      S.n_blocks = nb_all;
+      S.split1 = s1;
     }
   }
   __syncthreads();
+  if (S.split1 > 1) {
+    const int units = S.n_blocks * (kInter / 64);
+    for (int i = tid; i < units; i += kThreads) split_count[i] = 0;
+  }
 
   // Phase C: deterministic scatter, chunk by chunk.
   for (int base = 0; base < T; base += kThreads) {
@@ -163,7 +211,7 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
 }  // namespace
 
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
-                           int bn, const Layout& L, uint8_t* ws, cudaStream_t stream) {
+                           int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -173,13 +221,13 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
     if (err != cudaSuccess) return err;
     attr_set[dev] = true;
   }
-  permute_kernel<<<1, kThreads, smem, stream>>>(
+  return launch_pdl(permute_kernel, dim3(1), dim3(kThreads), smem, stream,
       topk_idx, topk_w, T, E_local, local_offset, bn, reinterpret_cast<int32_t*>(ws + L.expert_cnt),
       reinterpret_cast<int32_t*>(ws + L.expert_poff), reinterpret_cast<int32_t*>(ws + L.n_blocks),
       reinterpret_cast<int4*>(ws + L.blocks), L.max_blocks, reinterpret_cast<int32_t*>(ws + L.row_token),
       reinterpret_cast<float*>(ws + L.row_weight), reinterpret_cast<int32_t*>(ws + L.token_rows),
-      reinterpret_cast<uint32_t*>(ws + L.status));
-  return cudaGetLastError();
+      reinterpret_cast<uint32_t*>(ws + L.status), num_sms, reinterpret_cast<int32_t*>(ws + L.splits),
+      reinterpret_cast<int32_t*>(ws + L.split_count), L.split_items, L.pair_planes);
 }
 
 }  // namespace fbmoe

@@ -3,7 +3,8 @@
 // Reference counterpart: reduce_add_kernel_small/large (solution/triton/main.py:
 // 1604-1714), which adds bf16 pair rows with bf16 __hadd2.  Here the f16 pair
 // rows are summed in fp32 over the token's slots in fixed slot order
-// (deterministic) and rounded to bf16 once.  Tokens with no local expert get a zero row, as in the reference.
+// (deterministic) and rounded to bf16 once; when GEMM2 split its K (decode) the
+// planes of pair rows are added too, plane by plane.  Tokens with no local expert get a zero row, as in the reference.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -16,7 +17,10 @@ constexpr int kReduceChunks = kHidden / (kReduceThreads * 8);  // 7
 template <bool kF32Out>
 __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __restrict__ pair_out,
                                                                 const int32_t* __restrict__ token_rows,
-                                                                void* __restrict__ out_) {
+                                                                void* __restrict__ out_,
+                                                                const int32_t* __restrict__ splits,
+                                                                size_t plane_elems) {
+  pdl_wait();
   const int t = blockIdx.y;
   const int col = (blockIdx.x * kReduceThreads + threadIdx.x) * 8;
   float acc[8];
@@ -25,10 +29,13 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __
   const int4* rows4 = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
   const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
   const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+  const int planes = splits[1];  // GEMM2 K splits: one plane of pair rows each
+  for (int s = 0; s < planes; ++s)
 #pragma unroll
   for (int k = 0; k < kTopK; ++k) {
     if (rows[k] >= 0) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(pair_out + (size_t)rows[k] * kHidden + col));
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(pair_out + (size_t)s * plane_elems +
+                                                           (size_t)rows[k] * kHidden + col));
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -61,11 +68,11 @@ cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f
   dim3 grid(kReduceChunks, T);
   const __half* pairs = reinterpret_cast<const __half*>(ws + L.pair_out);
   const int32_t* rows = reinterpret_cast<const int32_t*>(ws + L.token_rows);
+  const int32_t* splits = reinterpret_cast<const int32_t*>(ws + L.splits);
+  const size_t plane = (size_t)L.pcap * kHidden;
   if (f32_out)
-    reduce_kernel<true><<<grid, kReduceThreads, 0, stream>>>(pairs, rows, out);
-  else
-    reduce_kernel<false><<<grid, kReduceThreads, 0, stream>>>(pairs, rows, out);
-  return cudaGetLastError();
+    return launch_pdl(reduce_kernel<true>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane);
+  return launch_pdl(reduce_kernel<false>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane);
 }
 
 }  // namespace fbmoe

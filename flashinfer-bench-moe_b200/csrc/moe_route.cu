@@ -167,6 +167,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) route_kernel(const float*
   __shared__ float sh_s[kWarpsPerBlock][kExperts];
   __shared__ int sh_sel[kWarpsPerBlock][kTopK];
 
+  pdl_wait();
+  pdl_trigger();
   if (blockIdx.x == 0 && threadIdx.x == 0 && status != nullptr) status[0] = 0u;
 
   const int warp = threadIdx.x >> 5;
@@ -370,9 +372,8 @@ cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, floa
   if (T <= 0) return cudaSuccess;
   int blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  route_kernel<<<blocks, kWarpsPerBlock * 32, 0, stream>>>(
-      logits, reinterpret_cast<const __nv_bfloat16*>(bias_bf16), T, scale, topk_idx, topk_w, status);
-  return cudaGetLastError();
+  return launch_pdl(route_kernel, dim3(blocks), dim3(kWarpsPerBlock * 32), 0, stream, logits,
+                    reinterpret_cast<const __nv_bfloat16*>(bias_bf16), T, scale, topk_idx, topk_w, status);
 }
 
 }  // namespace fbmoe
