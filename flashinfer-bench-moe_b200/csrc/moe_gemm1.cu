@@ -431,8 +431,6 @@ cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, 
   (void)E_local;
   switch (bn) {
     case 16: return launch_g1<16>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
-    case 32: return launch_g1<32>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
-    case 64: return launch_g1<64>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
     case 128:
       return launch_gemm1_rows(tm_w1, tm_aperm, reinterpret_cast<const float*>(ws + L.a_scale_perm), w1_scale, L, ws,
                                num_sms, stream);

@@ -388,8 +388,6 @@ cudaError_t launch_gemm2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, 
   (void)E_local;
   switch (bn) {
     case 16: return launch_g2<16>(tm_w2, tm_inter, w2_scale, L, ws, num_sms, stream);
-    case 32: return launch_g2<32>(tm_w2, tm_inter, w2_scale, L, ws, num_sms, stream);
-    case 64: return launch_g2<64>(tm_w2, tm_inter, w2_scale, L, ws, num_sms, stream);
     case 128: return launch_g2<128>(tm_w2, tm_inter, w2_scale, L, ws, num_sms, stream);
     default: return cudaErrorInvalidValue;
   }
