@@ -198,25 +198,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int4 blk = blocks[u / kTiles];
       const int j = u % kTiles;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
-      const bool live = row < nrows;
       const float* ws1 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + j) * kHBlocks;
       const float* ws2 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + kIBlocks + j) * kHBlocks;
-      // Row scales: 56 contiguous floats, read 4 K-blocks at a time, one group
-      // ahead.  W1 scales: lane l holds K-blocks l and 32+l, picked by shuffle.
-      const float4* asc4 = reinterpret_cast<const float4*>(a_scale_perm + (size_t)(live ? r0 + row : 0) * kHBlocks);
+      // Row scales: one scalar load per K-block, issued a K-block ahead (rows past
+      // the block's end read row 0's scales; their results are never stored).
+      // W1 scales: lane l holds K-blocks l and 32+l, picked by shuffle.
+      const float* asp = a_scale_perm + (size_t)(r0 + (row < nrows ? row : 0)) * kHBlocks;
       const float w1a = __ldg(ws1 + lane), w1b = lane < kHBlocks - 32 ? __ldg(ws1 + 32 + lane) : 0.0f;
       const float w2a = __ldg(ws2 + lane), w2b = lane < kHBlocks - 32 ? __ldg(ws2 + 32 + lane) : 0.0f;
-      float acc[64];
+      // packed accumulators: acc[k] = columns (2k, 2k+1) of this warp's 32 first-half
+      // columns (k < 16) or second-half columns (k >= 16)
+      uint64_t acc[32];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
-      float4 a_cur = __ldg(asc4), a_nxt = __ldg(asc4 + 1);
+      for (int i = 0; i < 32; ++i) acc[i] = 0ull;
+      float a_next = __ldg(asp);
       for (int kb = 0; kb < kHBlocks; ++kb) {
-        if ((kb & 3) == 0 && kb > 0) {
-          a_cur = a_nxt;
-          if (kb + 4 < kHBlocks) a_nxt = __ldg(asc4 + (kb >> 2) + 1);
-        }
-        const float a_pick = (kb & 3) == 0 ? a_cur.x : (kb & 3) == 1 ? a_cur.y : (kb & 3) == 2 ? a_cur.z : a_cur.w;
-        const float a_s = live ? a_pick : 0.0f;
+        const float a_s = a_next;
+        if (kb + 1 < kHBlocks) a_next = __ldg(asp + kb + 1);
         const float w_1 = __shfl_sync(0xffffffffu, kb < 32 ? w1a : w1b, kb & 31);
         const float w_2 = __shfl_sync(0xffffffffu, kb < 32 ? w2a : w2b, kb & 31);
         const uint32_t buf = kbg & 1u;
@@ -227,16 +225,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t t0 = tmem_base + lane_base + buf * 256 + 32 * g;
-        const float f1 = a_s * w_1, f2 = a_s * w_2;
+        const uint64_t f1 = f32x2_pack(a_s * w_1, a_s * w_1), f2 = f32x2_pack(a_s * w_2, a_s * w_2);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           // chunks 0-1: first-half columns (f1); 2-3: second half (f2)
-          float p[16];
-          tmem_ld16(t0 + (c < 2 ? 16 * c : 128 + 16 * (c - 2)), p);
+          uint64_t p[8];
+          tmem_ld16_pairs(t0 + (c < 2 ? 16 * c : 128 + 16 * (c - 2)), p);
           tmem_wait_ld();
-          const float f = c < 2 ? f1 : f2;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(p[i], f, acc[16 * c + i]);
+          for (int i = 0; i < 8; ++i) f32x2_fma(acc[8 * c + i], p[i], c < 2 ? f1 : f2);
         }
         tc_fence_before();
         __syncwarp();
@@ -252,10 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t w[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
-            const int c = 8 * v + 2 * h;
-            const float x2a = acc[32 + c], x2b = acc[32 + c + 1];
-            const float ya = x2a / (1.0f + expf(-x2a)) * acc[c];
-            const float yb = x2b / (1.0f + expf(-x2b)) * acc[c + 1];
+            const int k = 4 * v + h;  // columns 2k, 2k+1
+            float x1a, x1b, x2a, x2b;
+            f32x2_unpack(acc[k], x1a, x1b);
+            f32x2_unpack(acc[16 + k], x2a, x2b);
+            const float ya = x2a / (1.0f + expf(-x2a)) * x1a;
+            const float yb = x2b / (1.0f + expf(-x2b)) * x1b;
             const __half ha = to_half_sat(ya, sat), hb = to_half_sat(yb, sat);
             w[h] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
           }
