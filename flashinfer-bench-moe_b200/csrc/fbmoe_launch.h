@@ -39,6 +39,7 @@ struct Layout {
   size_t row_weight;   // fp32[pcap]
   size_t inter;        // f16[pcap * 2048]   SwiGLU output, expert-contiguous rows
   size_t pair_out;     // f16[pcap * 7168]   weighted per-(token, expert) rows
+  size_t chunk_cnt;    // int32[ceil(T/1024) * E_local] per-chunk expert counts (multi-CTA permute)
   size_t a_perm;       // e4m3[pcap * 7168]  token rows in permuted order (128-row blocks only)
   size_t splits;       // int32[2]: K splits of GEMM1 / GEMM2, chosen on the device per call
   size_t split_count;  // int32[kSplitItems]: arrivals per GEMM1 unit (split-K fix-up)

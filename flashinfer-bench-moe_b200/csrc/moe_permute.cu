@@ -15,9 +15,15 @@
 // It also chooses the K splits of the decode GEMMs for this call from the block
 // count (see pick_split) and clears the split-K arrival counters.
 //
-// One CTA of 1024 threads; tokens are processed in chunks of 1024.  Within a
-// chunk, a token's rank inside an expert is the number of set bits before it
-// in that expert's 1024-bit membership mask, which is order-independent.
+// Tokens are processed in chunks of 1024, one CTA of 1024 threads per chunk.
+// With one chunk (T <= 1024) a single CTA counts, scans and scatters.  With more,
+// permute_count_kernel first writes each chunk's per-expert counts; then every
+// scatter CTA derives the expert offsets (redundantly, from the small count
+// matrix) and its own chunk's starting row inside each expert, so rows stay
+// token-ascending across chunks.  CTA 0 alone writes the per-expert tables and
+// the block list.  Within a chunk, a token's rank inside an expert is the number
+// of set bits before it in that expert's 1024-bit membership mask, which is
+// order-independent.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -33,7 +39,6 @@ struct PermuteSmem {
   int poff[kMaxLocal + 1];
   int bstart[kMaxLocal + 1];
   int cursor[kMaxLocal];
-  int chunk_total[kMaxLocal];
   uint32_t bits[kMaxLocal][kWordsPerChunk];
   uint16_t wpre[kMaxLocal][kWordsPerChunk];
   int scan_tmp[2][kMaxLocal / 32];
@@ -60,6 +65,28 @@ __device__ int pick_split(int units, int sms, const int* cand, int ncand, int ma
     }
   }
   return best;
+}
+
+// Per-chunk expert counts: CTA c counts tokens [1024c, 1024c + 1024).
+__global__ void __launch_bounds__(kThreads) permute_count_kernel(const int32_t* __restrict__ topk_idx, int T,
+                                                                int E_local, int local_offset,
+                                                                int32_t* __restrict__ chunk_cnt) {
+  __shared__ int cnt[kMaxLocal];
+  const int tid = threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  if (tid < kMaxLocal) cnt[tid] = 0;
+  __syncthreads();
+  const int t = blockIdx.x * kThreads + tid;
+  if (t < T) {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int e = topk_idx[(size_t)t * kTopK + k] - local_offset;
+      if ((unsigned)e < (unsigned)E_local) atomicAdd(&cnt[e], 1);
+    }
+  }
+  __syncthreads();
+  if (tid < E_local) chunk_cnt[(size_t)blockIdx.x * E_local + tid] = cnt[tid];
 }
 
 // Exclusive scan of one value per thread over threads 0..255 (8 warps).
@@ -95,7 +122,8 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
                                                           uint32_t* __restrict__ status, int num_sms,
                                                           int32_t* __restrict__ splits,
                                                           int32_t* __restrict__ split_count, int split_items,
-                                                          int pair_planes) {
+                                                          int pair_planes, const int32_t* __restrict__ chunk_cnt,
+                                                          int n_chunks) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   PermuteSmem& S = *reinterpret_cast<PermuteSmem*>(smem_raw);
   const int tid = threadIdx.x;
@@ -103,16 +131,34 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
 
   pdl_wait();
   pdl_trigger();
-  for (int e = tid; e < kMaxLocal; e += kThreads) S.count[e] = 0;
-  __syncthreads();
+  const int chunk = blockIdx.x;
+  const bool lead = chunk == 0;  // writes the per-expert tables and the block list
 
-  // Phase A: counts.
-  for (int t = tid; t < T; t += kThreads) {
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      const int e = topk_idx[(size_t)t * kTopK + k] - local_offset;
-      if ((unsigned)e < (unsigned)E_local) atomicAdd(&S.count[e], 1);
+  // Phase A: per-expert totals, and this chunk's starting rank inside each expert.
+  if (n_chunks == 1) {
+    for (int e = tid; e < kMaxLocal; e += kThreads) {
+      S.count[e] = 0;
+      S.cursor[e] = 0;
     }
+    __syncthreads();
+    for (int t = tid; t < T; t += kThreads) {
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        const int e = topk_idx[(size_t)t * kTopK + k] - local_offset;
+        if ((unsigned)e < (unsigned)E_local) atomicAdd(&S.count[e], 1);
+      }
+    }
+  } else if (tid < kMaxLocal) {
+    int tot = 0, pre = 0;
+    if (tid < E_local) {
+      for (int c = 0; c < n_chunks; ++c) {
+        const int v = chunk_cnt[(size_t)c * E_local + tid];
+        pre += c < chunk ? v : 0;
+        tot += v;
+      }
+    }
+    S.count[tid] = tot;
+    S.cursor[tid] = pre;
   }
   __syncthreads();
 
@@ -127,16 +173,18 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
     const int boff = block_excl_scan_256(nb, S.scan_tmp[1], &tot_blocks);
     if (e < E_local) {
       S.poff[e] = off;
-      S.cursor[e] = off;
-      expert_cnt[e] = c;
-      expert_poff[e] = off;
-      for (int j = 0; j < nb; ++j) {
-        const int b = boff + j;
-        if (b < max_blocks) blocks[b] = make_int4(e, off + j * bn, min(bn, c - j * bn), 0);
+      S.cursor[e] += off;
+      if (lead) {
+        expert_cnt[e] = c;
+        expert_poff[e] = off;
+        for (int j = 0; j < nb; ++j) {
+          const int b = boff + j;
+          if (b < max_blocks) blocks[b] = make_int4(e, off + j * bn, min(bn, c - j * bn), 0);
+        }
+        for (int r = off + c; r < off + padded; ++r) row_token[r] = -1;  // padding rows
       }
-      for (int r = off + c; r < off + padded; ++r) row_token[r] = -1;  // padding rows
     }
-    if (e == 0) {
+    if (e == 0 && lead) {
       expert_poff[E_local] = tot_rows;
       const int nb_all = min(tot_blocks, max_blocks);
       *n_blocks = nb_all;
@@ -156,16 +204,16 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
     }
   }
   __syncthreads();
-  if (S.split1 > 1) {
+  if (lead && S.split1 > 1) {
     const int units = S.n_blocks * (kInter / 64);
     for (int i = tid; i < units; i += kThreads) split_count[i] = 0;
   }
 
-  // Phase C: deterministic scatter, chunk by chunk.
-  for (int base = 0; base < T; base += kThreads) {
+  // Phase C: deterministic scatter of this chunk.
+  {
     for (int i = tid; i < kMaxLocal * kWordsPerChunk; i += kThreads) (&S.bits[0][0])[i] = 0u;
     __syncthreads();
-    const int t = base + tid;
+    const int t = chunk * kThreads + tid;
     int le[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
@@ -185,7 +233,6 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
         S.wpre[tid][w] = (uint16_t)run;
         run += __popc(S.bits[tid][w]);
       }
-      S.chunk_total[tid] = run;
     }
     __syncthreads();
     if (t < T) {
@@ -202,9 +249,6 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
         token_rows[(size_t)t * kTopK + k] = row;
       }
     }
-    __syncthreads();
-    if (tid < E_local) S.cursor[tid] += S.chunk_total[tid];
-    __syncthreads();
   }
 }
 
@@ -221,13 +265,21 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
     if (err != cudaSuccess) return err;
     attr_set[dev] = true;
   }
-  return launch_pdl(permute_kernel, dim3(1), dim3(kThreads), smem, stream,
+  const int n_chunks = (T + kThreads - 1) / kThreads;
+  int32_t* chunk_cnt = reinterpret_cast<int32_t*>(ws + L.chunk_cnt);
+  if (n_chunks > 1) {
+    cudaError_t err = launch_pdl(permute_count_kernel, dim3(n_chunks), dim3(kThreads), 0, stream, topk_idx, T,
+                                 E_local, local_offset, chunk_cnt);
+    if (err != cudaSuccess) return err;
+  }
+  return launch_pdl(permute_kernel, dim3(n_chunks > 0 ? n_chunks : 1), dim3(kThreads), smem, stream,
       topk_idx, topk_w, T, E_local, local_offset, bn, reinterpret_cast<int32_t*>(ws + L.expert_cnt),
       reinterpret_cast<int32_t*>(ws + L.expert_poff), reinterpret_cast<int32_t*>(ws + L.n_blocks),
       reinterpret_cast<int4*>(ws + L.blocks), L.max_blocks, reinterpret_cast<int32_t*>(ws + L.row_token),
       reinterpret_cast<float*>(ws + L.row_weight), reinterpret_cast<int32_t*>(ws + L.token_rows),
       reinterpret_cast<uint32_t*>(ws + L.status), num_sms, reinterpret_cast<int32_t*>(ws + L.splits),
-      reinterpret_cast<int32_t*>(ws + L.split_count), L.split_items, L.pair_planes);
+      reinterpret_cast<int32_t*>(ws + L.split_count), L.split_items, L.pair_planes,
+      static_cast<const int32_t*>(chunk_cnt), n_chunks);
 }
 
 }  // namespace fbmoe

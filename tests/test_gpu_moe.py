@@ -115,8 +115,9 @@ def test_forward_is_deterministic(workloads, entry, gpu_weights32):
     assert torch.equal(a, b)
 
 
-def test_permutation_invariants(oracle_mod, fbmoe_lib, workloads, entry, gpu_weights32):
-    T, E = 901, 32
+@pytest.mark.parametrize("T", [901, 3000])  # one 1024-token chunk; three chunks (multi-CTA permute)
+def test_permutation_invariants(oracle_mod, fbmoe_lib, workloads, entry, gpu_weights32, T):
+    E = 32
     inp = workloads.make_inputs(T, seed=9, config="standard", device="cuda", weights=gpu_weights32)
     _run(entry, workloads, inp)
     lay = fbmoe_lib.workspace_layout(T, E)
