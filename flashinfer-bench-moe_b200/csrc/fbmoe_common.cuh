@@ -192,6 +192,16 @@ __device__ __forceinline__ void tma_load_2d_nohint(void* smem_dst, const CUtenso
 }
 
 // L2 eviction policies (createpolicy).
+// 1-D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16),
+// completing as transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -44,7 +44,7 @@ struct Layout {
   size_t splits;       // int32[2]: K splits of GEMM1 / GEMM2, chosen on the device per call
   size_t split_count;  // int32[kSplitItems]: arrivals per GEMM1 unit (split-K fix-up)
   size_t split_part;   // fp32[kSplitItems][128][16]: GEMM1 split partial sums
-  size_t a_scale_perm; // fp32[pcap * 56]    their 1x128 scales, row-major (128-row blocks only)
+  size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
   size_t total;        // bytes
   int pcap;            // row capacity (multiple of 128)
   int e_local;         // local experts the layout was made for
@@ -61,8 +61,8 @@ constexpr int kSplitItems = 1024;
 constexpr int kMaxPairPlanes = 4;
 int choose_block_rows(int T, int E_local);
 
-// Copies each routed token's row (and its 56 scales, row-major) to its permuted
-// position, for the 128-row-block GEMM1 that loads A with plain TMA boxes.
+// Copies each routed token's row (and its 56 scales, [K-block][row]) to its
+// permuted position, for the 128-row-block GEMM1 that loads A with plain TMA boxes.
 cudaError_t launch_gather_rows(const uint8_t* hidden, const float* hidden_scale, int T, const Layout& L,
                                uint8_t* ws, cudaStream_t stream);
 
@@ -76,13 +76,15 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
                            int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream);
 
 // GEMM1 + SwiGLU: inter[row, :] for every local (token, expert) row.
-// tm_aperm: the permuted activation rows (a_perm) in 128-row boxes (used for block_rows 128).
-cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const uint8_t* hidden, const float* hidden_scale, int T,
+// tm_aperm: the permuted activation rows (a_perm) in 128-row boxes, tm_ascale: their
+// scales in 128-row x 1-K-block boxes (both used for block_rows 128 only).
+cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
+                         const uint8_t* hidden, const float* hidden_scale, int T,
                          const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
                          cudaStream_t stream);
 
 // GEMM1 + SwiGLU for blocks of 128 rows with the tokens as the MMA M operand.
-cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const float* a_scale_perm,
+cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
                               const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
                               cudaStream_t stream);
 

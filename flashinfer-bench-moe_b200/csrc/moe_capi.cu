@@ -196,7 +196,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   const int bn = choose_block_rows(T, E_local);
   const int sms = num_sms_of_current_device();
 
-  CUtensorMap tm_w1, tm_w2, tm_inter, tm_w2raw, tm_aperm;
+  CUtensorMap tm_w1, tm_w2, tm_inter, tm_w2raw, tm_aperm, tm_ascale;
   int rc = encode_2d(&tm_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm1_weights, kHidden, (uint64_t)E_local * kGemm1N,
                      128, 64);
   if (rc) return rc;
@@ -205,6 +205,10 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   if (rc) return rc;
   if (bn == 128) {
     rc = encode_2d(&tm_aperm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + L.a_perm, kHidden, (uint64_t)L.pcap, 128, 128);
+    if (rc) return rc;
+    // [56][pcap] fp32 scales: one box = 128 consecutive rows of one K-block (512 bytes)
+    rc = encode_2d(&tm_ascale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.a_scale_perm, (uint64_t)L.pcap, kHBlocks,
+                   128, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
   // W2 in 64-byte (64-K) slices of 256 rows, unswizzled: converted on chip by GEMM2.
@@ -234,7 +238,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
     e = launch_gather_rows(reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, L, ws, stream);
     if (e != cudaSuccess) return from_cuda(e);
   }
-  e = launch_gemm1(&tm_w1, &tm_aperm, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
+  e = launch_gemm1(&tm_w1, &tm_aperm, &tm_ascale, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
                    gemm1_weights_scale, E_local, bn, L, ws, sms, stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 3, stream);

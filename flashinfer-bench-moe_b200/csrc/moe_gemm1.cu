@@ -425,14 +425,15 @@ cudaError_t launch_g1(const CUtensorMap* tm, const uint8_t* hidden, const float*
 
 }  // namespace
 
-cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const uint8_t* hidden, const float* hidden_scale, int T,
+cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
+                         const uint8_t* hidden, const float* hidden_scale, int T,
                          const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
                          cudaStream_t stream) {
   (void)E_local;
   switch (bn) {
     case 16: return launch_g1<16>(tm_w1, hidden, hidden_scale, T, w1_scale, L, ws, num_sms, stream);
     case 128:
-      return launch_gemm1_rows(tm_w1, tm_aperm, reinterpret_cast<const float*>(ws + L.a_scale_perm), w1_scale, L, ws,
+      return launch_gemm1_rows(tm_w1, tm_aperm, tm_ascale, w1_scale, L, ws,
                                num_sms, stream);
     default: return cudaErrorInvalidValue;
   }

@@ -41,17 +41,20 @@ constexpr int kBBytes = 256 * 128;               // 32 KB of W1 rows
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStages * kABytes;
-constexpr int kOffBar = kOffB + kStages * kBBytes;
-constexpr int kNumBars = 2 * kStages + 4 + 1;
+constexpr int kScaleSlots = 8;                   // ring of per-K-block row-scale vectors
+constexpr int kOffAS = kOffB + kStages * kBBytes;            // fp32 [8][128] row scales
+constexpr int kOffWS = kOffAS + kScaleSlots * kRows * 4;    // fp32 [2][112] W1 scales of a unit
+constexpr int kOffBar = kOffWS + 2 * 2 * kHBlocks * 4;
+constexpr int kNumBars = 2 * kStages + 4 + 1 + kScaleSlots + 2;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory over the per-CTA limit");
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm1_rows_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_aperm,
-                      const float* __restrict__ a_scale_perm, const float* __restrict__ w1_scale,
+                      const __grid_constant__ CUtensorMap tm_ascale, const float* __restrict__ w1_scale,
                       const int32_t* __restrict__ n_blocks_ptr, const int4* __restrict__ blocks,
-                      const int32_t* __restrict__ row_token, __half* __restrict__ inter,
+                      __half* __restrict__ inter,
                       uint32_t* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -63,6 +66,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = bars + 2 * kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tfull + 4;
+  uint64_t* sfull = drain + 1;               // row scales of K-block x landed in slot x % 8
+  uint64_t* wfull = sfull + kScaleSlots;     // W1 scales of a unit landed in slot (unit % 2)
+  float* sAS = reinterpret_cast<float*>(sm + kOffAS);
+  float* sWS = reinterpret_cast<float*>(sm + kOffWS);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + kOffMisc);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sm + kOffMisc + 4);
 
@@ -79,12 +86,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], kEpiWarps);  // one arrive per epilogue warp
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < kScaleSlots; ++s) mbar_init(&sfull[s], 1);
+    mbar_init(&wfull[0], 1);
+    mbar_init(&wfull[1], 1);
     *sAbort = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w1);
     tma_prefetch_desc(&tm_aperm);
+    tma_prefetch_desc(&tm_ascale);
   }
   if (warp == 1) {
     tmem_alloc(sTmem, 512);
@@ -106,22 +117,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Operand tiles into stage x % 4, the K-block's 128 row scales into slot
+    // x % 8 and, at a unit's first K-block, its W1 scales into slot unit % 2.
+    // Slot reuse is safe without extra barriers: loads for K-block x start only
+    // after MMA x - 4 completed, which needed the epilogue done with x - 6 (two
+    // TMEM buffers); slot x % 8 last held x - 8, and unit slots are 56 K-blocks apart.
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     uint32_t issued_mask = 0, parity_mask = 0;  // per stage: ever issued / parity of the last issue
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    int x = 0, ui = 0;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ui) {
       const int4 blk = blocks[u / kTiles];
       const int j = u % kTiles;
       const int e = blk.x, r0 = blk.y;
       const int wrow = e * kGemm1N + 128 * j;
-      for (int kb = 0; kb < kHBlocks; ++kb) {
+      for (int kb = 0; kb < kHBlocks; ++kb, ++x) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutProducer);
           break;
         }
         if (lane == 0) {
+          if (kb == 0) {
+            uint64_t* wb = &wfull[ui & 1];
+            float* wdst = sWS + (ui & 1) * 2 * kHBlocks;
+            mbar_arrive_expect_tx(wb, 2 * kHBlocks * 4);
+            bulk_load_1d(wdst, w1_scale + ((size_t)e * (kGemm1N / kBlk) + j) * kHBlocks, kHBlocks * 4, wb);
+            bulk_load_1d(wdst + kHBlocks, w1_scale + ((size_t)e * (kGemm1N / kBlk) + kIBlocks + j) * kHBlocks,
+                         kHBlocks * 4, wb);
+          }
+          uint64_t* sb = &sfull[x & (kScaleSlots - 1)];
+          mbar_arrive_expect_tx(sb, kRows * 4);
+          tma_load_2d_nohint(sAS + (x & (kScaleSlots - 1)) * kRows, &tm_ascale, sb, r0, kb);
           mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes);
           tma_load_2d_nohint(sA + stage * kABytes, &tm_aperm, &full[stage], kb * kBlk, r0);
           uint8_t* b = sB + stage * kBBytes;
@@ -145,6 +173,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((issued_mask >> s) & 1u)
           if (!mbar_wait(&full[s], (parity_mask >> s) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
             fail(kStatusTimeoutDrain);
+      for (int k = 1; k <= kScaleSlots && k <= x; ++k) {
+        const int y = x - k;  // the last K-blocks issued, one per slot
+        if (!mbar_wait(&sfull[y & (kScaleSlots - 1)], (uint32_t)(y >> 3) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+          fail(kStatusTimeoutDrain);
+      }
+      for (int k = 1; k <= 2 && k <= ui; ++k) {
+        const int v = ui - k;
+        if (!mbar_wait(&wfull[v & 1], (uint32_t)(v >> 1) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+          fail(kStatusTimeoutDrain);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -194,29 +232,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t kbg = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+    int ui = 0;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ui) {
       const int4 blk = blocks[u / kTiles];
       const int j = u % kTiles;
-      const int e = blk.x, r0 = blk.y, nrows = blk.z;
-      const float* ws1 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + j) * kHBlocks;
-      const float* ws2 = w1_scale + ((size_t)e * (kGemm1N / kBlk) + kIBlocks + j) * kHBlocks;
-      // Row scales: one scalar load per K-block, issued a K-block ahead (rows past
-      // the block's end read row 0's scales; their results are never stored).
-      // W1 scales: lane l holds K-blocks l and 32+l, picked by shuffle.
-      const float* asp = a_scale_perm + (size_t)(r0 + (row < nrows ? row : 0)) * kHBlocks;
-      const float w1a = __ldg(ws1 + lane), w1b = lane < kHBlocks - 32 ? __ldg(ws1 + 32 + lane) : 0.0f;
-      const float w2a = __ldg(ws2 + lane), w2b = lane < kHBlocks - 32 ? __ldg(ws2 + 32 + lane) : 0.0f;
+      const int r0 = blk.y, nrows = blk.z;
+      // this unit's W1 scales: [0, 56) first half, [56, 112) second half
+      if (!mbar_wait(&wfull[ui & 1], (uint32_t)(ui >> 1) & 1u, sAbort, kWaitBudgetNs)) {
+        if (lane == 0) fail(kStatusTimeoutEpilogue);
+        break;
+      }
+      const float* wsu = sWS + (ui & 1) * 2 * kHBlocks;
       // packed accumulators: acc[k] = columns (2k, 2k+1) of this warp's 32 first-half
       // columns (k < 16) or second-half columns (k >= 16)
       uint64_t acc[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) acc[i] = 0ull;
-      float a_next = __ldg(asp);
       for (int kb = 0; kb < kHBlocks; ++kb) {
-        const float a_s = a_next;
-        if (kb + 1 < kHBlocks) a_next = __ldg(asp + kb + 1);
-        const float w_1 = __shfl_sync(0xffffffffu, kb < 32 ? w1a : w1b, kb & 31);
-        const float w_2 = __shfl_sync(0xffffffffu, kb < 32 ? w2a : w2b, kb & 31);
+        const uint32_t slot = kbg & (kScaleSlots - 1);
+        if (!mbar_wait(&sfull[slot], (kbg >> 3) & 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutEpilogue);
+          break;
+        }
+        // rows past the block's end use whatever scale the box held (zero-filled
+        // past the buffer); their results are never stored
+        const float a_s = sAS[slot * kRows + row];
+        const float w_1 = wsu[kb], w_2 = wsu[kHBlocks + kb];
         const uint32_t buf = kbg & 1u;
         if (!mbar_wait(&tfull[buf], (kbg >> 1) & 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
@@ -275,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const float* a_scale_perm,
+cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
                               const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
                               cudaStream_t stream) {
   static bool attr_set[64] = {false};
@@ -290,9 +332,8 @@ cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_ap
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;
   return launch_pdl(gemm1_rows_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, *tm_w1, *tm_aperm,
-                    a_scale_perm, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
-                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<const int32_t*>(ws + L.row_token),
-                    reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
+                    *tm_ascale, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
+                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
 }
 
 }  // namespace fbmoe

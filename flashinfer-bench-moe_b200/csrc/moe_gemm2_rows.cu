@@ -18,7 +18,9 @@
 // worst element at 0.35x the output tolerance, the same as one fp32 rounding.
 //
 // Warp roles (512 threads): w0 W2 producer (TMA, raw FP8, 16 KB per step),
-// w1 MMA issuer + TMEM owner, w2 intermediate producer (TMA), w3 idle,
+// w1 MMA issuer + TMEM owner, w2 intermediate producer (TMA, its own 4-slot
+// ring: with the slots tied to the 2-slot conversion ring, the intermediate
+// tile's load latency was exposed every step), w3 idle,
 // w4-w11 converters (256 threads, 4 x 16-byte chunks each per step),
 // w12-w15 epilogue (TMEM lane quarter = warp % 4).
 #include <math.h>
@@ -36,6 +38,7 @@ constexpr int kNTiles = kHidden / kN;         // 28
 constexpr int kKSteps = kInter / 64;          // 32 steps of 64
 constexpr int kRawStages = 4;
 constexpr int kConvStages = 2;
+constexpr int kAStages = 4;                   // intermediate tiles in flight (their TMA latency is exposed otherwise)
 constexpr int kRawBytes = kN * 64;            // 16 KB fp8
 constexpr int kWBytes = kN * 128;             // 32 KB f16 W2 operand
 constexpr int kABytes = kRows * 128;          // 16 KB f16 intermediate operand
@@ -43,8 +46,8 @@ constexpr uint64_t kWaitBudgetNs = 4000000000ull;
 constexpr int kOffRaw = 0;
 constexpr int kOffW = kOffRaw + kRawStages * kRawBytes;
 constexpr int kOffA = kOffW + kConvStages * kWBytes;
-constexpr int kOffBar = kOffA + kConvStages * kABytes;
-constexpr int kNumBars = 2 * kRawStages + 3 * kConvStages + 4 + 1;
+constexpr int kOffBar = kOffA + kAStages * kABytes;
+constexpr int kNumBars = 2 * kRawStages + 2 * kConvStages + 2 * kAStages + 4 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory over the per-CTA limit");
@@ -88,9 +91,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = bars + kRawStages;
   uint64_t* w_full = bars + 2 * kRawStages;                    // converters wrote the f16 W2 slot
-  uint64_t* a_full = bars + 2 * kRawStages + kConvStages;      // intermediate rows landed
-  uint64_t* c_empty = bars + 2 * kRawStages + 2 * kConvStages; // MMA done with the slot
-  uint64_t* tfull = bars + 2 * kRawStages + 3 * kConvStages;
+  uint64_t* c_empty = bars + 2 * kRawStages + kConvStages;     // MMA done with the f16 W2 slot
+  uint64_t* a_full = bars + 2 * kRawStages + 2 * kConvStages;  // intermediate rows landed
+  uint64_t* a_empty = a_full + kAStages;                       // MMA done with the intermediate slot
+  uint64_t* tfull = a_empty + kAStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tfull + 4;
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + kOffMisc);
@@ -106,8 +110,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kConvStages; ++s) {
       mbar_init(&w_full[s], 8);
-      mbar_init(&a_full[s], 1);
       mbar_init(&c_empty[s], 1);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -148,9 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();
         fence_proxy_async_global();
       }
-      const int n = w2_side ? kRawStages : kConvStages;
+      const int n = w2_side ? kRawStages : kAStages;
       uint64_t* fullb = w2_side ? raw_full : a_full;
-      uint64_t* emptyb = w2_side ? raw_empty : c_empty;
+      uint64_t* emptyb = w2_side ? raw_empty : a_empty;
       Ring ring(n);
       bool ok = true;
       uint32_t issued_mask = 0, parity_mask = 0;
@@ -186,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, kRows, kN);  // f16 x f16 -> fp32
-      Ring ring(kConvStages);
+      Ring ring(kConvStages), ar(kAStages);
       uint32_t ug = 0;
       bool ok = true, any = false;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ug) {
@@ -200,19 +207,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem_base + buf * kN;
         for (int ks = 0; ks < kKSteps; ++ks) {
           if (!mbar_wait(&w_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs) ||
-              !mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
+              !mbar_wait(&a_full[ar.slot], ar.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + ring.slot * kABytes));
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + ar.slot * kABytes));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(sW + ring.slot * kWBytes));
 #pragma unroll
           for (int k = 0; k < 4; ++k) mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (ks | k) ? 1u : 0u);
           tc_commit(&c_empty[ring.slot]);
+          tc_commit(&a_empty[ar.slot]);
           any = true;
           ring.next();
+          ar.next();
         }
         if (!ok) break;
         tc_commit(&tfull[buf]);
