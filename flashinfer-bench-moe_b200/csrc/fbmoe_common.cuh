@@ -299,6 +299,22 @@ __device__ __forceinline__ void tmem_ld16_pairs(uint32_t taddr, uint64_t (&v)[8]
   for (int i = 0; i < 8; ++i) asm("mov.b64 %0, {%1, %2};" : "=l"(v[i]) : "r"(r[2 * i]), "r"(r[2 * i + 1]));
 }
 
+// W2 dequantisation to f16 (both GEMM2 kernels).  Per 128-row block of W2 the
+// kernels pick a power of two 2^k with max_k s2 * 2^k in [32, 64); each element
+// becomes f16(fp8) * f16(s2 * 2^k) in one HMUL2 (the fp8 value is exact in f16,
+// the product stays below 448 * 64) and the epilogue multiplies by 2^-k exactly.
+// This returns k for the 16 scales of one block.
+__device__ __forceinline__ int w2_block_exponent(const float* s16) {
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kIBlocks; ++i) m = fmaxf(m, fabsf(__ldg(s16 + i)));
+  if (!(m > 0.0f) || !isfinite(m)) return 0;
+  int ex;
+  frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
+  int k = 6 - ex;  // m * 2^k in [32, 64)
+  return k < -60 ? -60 : (k > 60 ? 60 : k);
+}
+
 // ---------------------------------------------------- packed fp32 (f32x2) ----
 // sm_100 executes two IEEE fp32 FMAs (round-to-nearest, the same result as two
 // fmaf calls) per fma.rn.f32x2 instruction; the promotion epilogues use it to

@@ -44,6 +44,8 @@ struct Layout {
   size_t splits;       // int32[2]: K splits of GEMM1 / GEMM2, chosen on the device per call
   size_t split_count;  // int32[kSplitItems]: arrivals per GEMM1 unit (split-K fix-up)
   size_t split_part;   // fp32[kSplitItems][128][16]: GEMM1 split partial sums
+  size_t blk_ready;    // int32[max_blocks]: GEMM1 slices published per block (decode kernel)
+  size_t slice_cnt;    // int32[56]: GEMM2 items finished per hidden slice (decode kernel)
   size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
   size_t total;        // bytes
   int pcap;            // row capacity (multiple of 128)
@@ -75,22 +77,18 @@ cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, floa
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
                            int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream);
 
-// GEMM1 + SwiGLU: inter[row, :] for every local (token, expert) row.
-// tm_aperm: the permuted activation rows (a_perm) in 128-row boxes, tm_ascale: their
-// scales in 128-row x 1-K-block boxes (both used for block_rows 128 only).
-cudaError_t launch_gemm1(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
-                         const uint8_t* hidden, const float* hidden_scale, int T,
-                         const float* w1_scale, int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms,
-                         cudaStream_t stream);
+// Decode (16-row blocks): GEMM1 + SwiGLU, GEMM2 x routing weight and the
+// per-token combine in one persistent kernel; writes out (bf16, or fp32 partial
+// sums with f32_out).
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
+                          const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
+                          const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
+                          cudaStream_t stream);
 
 // GEMM1 + SwiGLU for blocks of 128 rows with the tokens as the MMA M operand.
 cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
                               const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
                               cudaStream_t stream);
-
-// GEMM2 (W2 dequantised to f16 on chip) x routing weight -> pair_out rows.
-cudaError_t launch_gemm2(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter, const float* w2_scale,
-                         int E_local, int bn, const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream);
 
 // GEMM2 for blocks of 128 rows with the tokens as the MMA M operand; tm_w2raw
 // maps W2 as unswizzled 64-byte x 256-row boxes.

@@ -67,6 +67,8 @@ Layout make_layout(int T, int E_local, bool allow_split) {
   L.splits = take(16);
   L.split_count = take((size_t)L.split_items * 4);
   L.split_part = take((size_t)L.split_items * 128 * 16 * 4);
+  L.blk_ready = take((size_t)L.max_blocks * 4);
+  L.slice_cnt = take((size_t)(kHidden / 128) * 4);
   const bool big = bn == 128;
   L.chunk_cnt = take((tt + 1023) / 1024 * (size_t)el * 4);
   L.a_perm = take(big ? (size_t)pcap * kHidden : 0);
@@ -234,19 +236,25 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, sms, L, ws, stream);
   if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 2, stream);
-  if (bn == 128) {
+  if (bn == 16) {
+    // decode: GEMM1, GEMM2 and the combine run as one kernel (its time is the
+    // "gemm1" stage of the profile; "gemm2" and "combine" stay empty)
+    e = launch_decode(&tm_w1, &tm_w2, &tm_inter, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale,
+                      T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    prof_record(fwd, 3, stream);
+    prof_record(fwd, 4, stream);
+  } else {
     e = launch_gather_rows(reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, L, ws, stream);
     if (e != cudaSuccess) return from_cuda(e);
+    e = launch_gemm1_rows(&tm_w1, &tm_aperm, &tm_ascale, gemm1_weights_scale, L, ws, sms, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    prof_record(fwd, 3, stream);
+    e = launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    prof_record(fwd, 4, stream);
+    e = launch_reduce(T, L, ws, out, f32_out, stream);
   }
-  e = launch_gemm1(&tm_w1, &tm_aperm, &tm_ascale, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T,
-                   gemm1_weights_scale, E_local, bn, L, ws, sms, stream);
-  if (e != cudaSuccess) return from_cuda(e);
-  prof_record(fwd, 3, stream);
-  e = bn == 128 ? launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream)
-                : launch_gemm2(&tm_w2, &tm_inter, gemm2_weights_scale, E_local, bn, L, ws, sms, stream);
-  if (e != cudaSuccess) return from_cuda(e);
-  prof_record(fwd, 4, stream);
-  e = launch_reduce(T, L, ws, out, f32_out, stream);
   prof_record(fwd, 5, stream);
   return from_cuda(e);
 }

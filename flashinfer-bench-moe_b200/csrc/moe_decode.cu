@@ -1,0 +1,846 @@
+// moe_decode.cu -- the expert computation of a decode-sized call (16-row
+// blocks, T <= 64) as ONE persistent kernel: GEMM1 + SwiGLU, GEMM2 x routing
+// weight and the per-token combine (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Reference counterparts: gemm1_kernel + act_quant_kernel (solution/triton/
+// main.py:41-223, 1426-1602), gemm2_kernel (main.py:433-600) and
+// reduce_add_kernel (main.py:1604-1714).  Per local expert e, permuted row r
+// (token t) and hidden column h:
+//     G1[r, n]    = sum_k A[t, k] * a_scale[k/128, t] * W1[e, n, k] * s1[e, n/128, k/128]
+//     inter[r, j] = silu(G1[r, 2048 + j]) * G1[r, j]                 (f16, clamped)
+//     pair[r, h]  = w[r] * sum_j inter[r, j] * W2[e, h, j] * s2[e, h/128, j/128]   (f16)
+//     out[t, h]   = sum over t's local slots of pair[r, h]            (fp32 sum, bf16)
+// The intermediate is stored as f16 (not re-quantised to FP8, and not bf16):
+// against the reference's fp32 intermediate, FP8 re-quantisation puts about 10%
+// of output elements outside atol 1e-2 / rtol 2e-2, bf16 leaves the worst element
+// at ~1.0x the tolerance, f16 at ~0.35x.  Values beyond the f16 range are clamped
+// to +-65504 and flagged in the status word (kStatusSaturated).
+//
+// Why one kernel.  At decode sizes the call streams the active experts' weights
+// (44 MB each) and little else; separate GEMM1 / GEMM2 / combine launches cost a
+// grid drain, a launch and a prologue each, and GEMM2 could not start streaming
+// W2 before the last GEMM1 CTA retired.  Here every CTA runs its GEMM1 work items,
+// then its GEMM2 items: W2 tiles stream in at once, and only the intermediate
+// rows of a block wait for that block's 32 GEMM1 slices (a per-block counter
+// that GEMM1 raises after publishing them).  The combine of hidden slice h runs
+// in the CTA whose GEMM2 item for slice h arrives last on the slice's counter,
+// so no grid-wide barrier exists.  The grid is at most one CTA per SM with one
+// CTA resident per SM, and nothing in GEMM1 waits on GEMM2, so every wait ends;
+// every wait is also bounded in wall time.
+//
+// Orientation (swap-AB) in both GEMMs: weight rows are the MMA's M = 128 operand
+// and the <= 16 token rows of a block its N operand.
+//
+// GEMM1 phase.  Work unit = (block of 16 rows of one expert) x (slice g of 64
+// output columns); the A tile stacks W1 rows [64g, 64g+64) (h1 half) on rows
+// [2048+64g, 2048+64g+64) (silu half); the B tile gathers the block's token rows
+// with cp.async (no permuted copy of the activations).  Every 128-K block is
+// MMA'd into its own TMEM buffer and promoted by s1 * a_scale into fp32
+// registers (the per-128-K block scales are applied exactly).  Four sets of four
+// epilogue warps take the K-blocks kb = j (mod 4), so four K-blocks are in flight
+// in the epilogue; their partial sums are added in set order.  Split-K: when few
+// units exist the permute kernel sets splits[0] = S > 1; the S items of a unit
+// write fp32 partials and the item that arrives last adds them in split order.
+// Warps: w0 producer (TMA + cp.async), w1 MMA issuer, w2-w3 idle, w4-w19 epilogue.
+//
+// GEMM2 phase.  Work unit = (block) x (slice h of 128 hidden columns): A = 128
+// W2 rows, dequantised on chip to f16 (one HMUL2 by the power-of-two-shifted
+// f16 scale, see w2_block_exponent) by eight converter warps into the UMMA
+// layout; B = the block's f16 intermediate rows
+// (TMA).  TMEM accumulates the whole K = 2048 (no promotion: the scale is in the
+// operand).  Split-K: splits[1] = S > 1 shares a unit's 16 K-blocks among S items
+// that write separate planes of pair rows; the combine adds the planes.
+// Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 intermediate producer (TMA),
+// w4-w7 and w12-w15 converters, w8-w11 epilogue (+ combine), the rest idle.
+#include "fbmoe_common.cuh"
+#include "fbmoe_launch.h"
+
+namespace fbmoe {
+namespace {
+
+constexpr int BN = 16;                      // rows per block
+constexpr int kThreads = 640;               // 20 warps
+constexpr uint64_t kWaitBudgetNs = 4000000000ull;
+constexpr int kG1Slices = kInter / 64;      // 32 slices of 64 intermediate columns
+constexpr int kG2Slices = kHidden / 128;    // 56 slices of 128 hidden columns
+
+// ---- GEMM1 phase layout (offsets inside the shared region)
+constexpr int kSets = 4;                    // epilogue warp sets
+constexpr int kEpi1Threads = 128 * kSets;
+// TMEM partial buffers: all 512 columns, so the MMA can run up to 32 K-blocks
+// (two split-K items) ahead of the promotion epilogue, whose per-item fix-up
+// (partials to L2, fence, counter) would otherwise stall the weight stream.
+constexpr int kBufs1 = 32;
+constexpr int kStages1 = 8;
+// A stage's cp.async row copies are signalled complete kLag stages after they
+// are issued, so up to kLag stages of row copies are in flight.
+constexpr int kLag = kStages1 - 2;
+constexpr int kA1Bytes = 128 * 128;
+constexpr int kB1Bytes = BN * 128;
+constexpr int kXchStride = BN + 1;
+constexpr int kP1A = 0;
+constexpr int kP1B = kP1A + kStages1 * kA1Bytes;
+constexpr int kP1AScale = kP1B + kStages1 * kB1Bytes;
+constexpr int kP1WScale = kP1AScale + kHBlocks * BN * 4;
+constexpr int kP1Xch = kP1WScale + 2 * kHBlocks * 4;
+constexpr int kP1Tok = kP1Xch + kSets * 128 * kXchStride * 4;
+constexpr int kP1End = kP1Tok + BN * 4;
+// ---- GEMM2 phase layout
+constexpr int kRawStages = 4;
+constexpr int kConvStages = 3;
+constexpr int kBStages = 6;
+constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
+constexpr int kAhBytes = 2 * 128 * 128;     // f16 W2 tile (two 64-K halves)
+constexpr int kB2Bytes = BN * 256;          // f16 intermediate rows (two 64-K halves)
+// TMEM accumulators of GEMM2 items: 32 x 16 columns, so the MMA runs up to 32
+// items ahead of the epilogue (which publishes every item to L2 with a fence
+// and a counter before the next).
+constexpr int kBufs2 = 32;
+constexpr int kP2Raw = 0;
+constexpr int kP2Ah = kP2Raw + kRawStages * kRawBytes;
+constexpr int kP2B = kP2Ah + kConvStages * kAhBytes;
+constexpr int kP2End = kP2B + kBStages * kB2Bytes;
+constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
+// ---- barriers and flags (not reused across phases)
+constexpr int kNumBars1 = 2 * kStages1 + 2 * kBufs1 + 1;
+constexpr int kNumBars2 = 2 * kRawStages + 2 * kConvStages + 2 * kBStages + 2 * kBufs2 + 1;
+constexpr int kOffBar = kRegion;
+constexpr int kOffMisc = kOffBar + (kNumBars1 + kNumBars2) * 8;
+constexpr int kSmemBytes = kOffMisc + 32 + 1024;  // + alignment slack
+constexpr int kTmemCols = 512;                    // one CTA per SM holds all of TMEM
+static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
+static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
+static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
+static_assert(kBufs1 * BN <= kTmemCols && kBufs2 * BN <= kTmemCols, "TMEM allocation");
+
+struct DecodeArgs {
+  CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
+  CUtensorMap tm_w2;     // W2 rows x 2048 K, 128-byte x 128-row boxes
+  CUtensorMap tm_inter;  // inter rows x 2048 f16, 64-column x 16-row boxes
+  const uint8_t* hidden;
+  const float* hidden_scale;
+  const float* w1_scale;
+  const float* w2_scale;
+  const int32_t* n_blocks;
+  const int4* blocks;
+  const int32_t* row_token;
+  const float* row_weight;
+  const int32_t* token_rows;
+  const int32_t* splits;
+  int32_t* split_count;
+  float* split_part;
+  int32_t* blk_ready;
+  int32_t* slice_cnt;
+  __half* inter;
+  __half* pair_out;
+  void* out;
+  uint32_t* status;
+  size_t plane_elems;
+  int T;
+  int f32_out;
+};
+
+// Ring position: slot and phase parity of successive uses of a ring of n slots.
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  int n;
+  __device__ explicit Ring(int n_) : n(n_) {}
+  __device__ void next() {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ============================================================== GEMM1 phase
+__device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
+                                            int nb, volatile int* sAbort, volatile int* sLast) {
+  constexpr int S = kStages1;
+  uint8_t* sA = sm + kP1A;
+  uint8_t* sB = sm + kP1B;
+  float* sAScale = reinterpret_cast<float*>(sm + kP1AScale);  // [56][BN]
+  float* sWScale = reinterpret_cast<float*>(sm + kP1WScale);  // [2][56]
+  float* sXch = reinterpret_cast<float*>(sm + kP1Xch);        // [sets][128][BN+1] partial sums
+  int* sTok = reinterpret_cast<int*>(sm + kP1Tok);            // [BN]
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = tfull + kBufs1;
+  uint64_t* drain = tempty + kBufs1;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_units = nb * kG1Slices;
+  const int n_split = a.splits[0];               // K splits per unit
+  const int nk = kHBlocks / n_split;             // K-blocks per work item
+  const int n_items = n_units * n_split;
+  auto fail = [&](uint32_t bit) {
+    *sAbort = 1;
+    atomicOr(a.status, bit);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol_w = l2_policy_evict_first();  // each weight tile is read about once
+    int stage = 0;
+    uint32_t phase = 0;
+    long issued = 0;
+    bool ok = true;
+    uint32_t last_parity[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) last_parity[s] = 0xFFFFFFFFu;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int u = it / n_split, sp = it % n_split;
+      const int4 blk = a.blocks[u / kG1Slices];
+      const int g = u % kG1Slices;
+      const int e = blk.x, r0 = blk.y, nrows = blk.z;
+      // token row pointers for the rows this lane copies: rows (lane>>3) + 4j
+      constexpr int kRowsPerLane = BN / 4;
+      const uint8_t* src[kRowsPerLane];
+#pragma unroll
+      for (int j = 0; j < kRowsPerLane; ++j) {
+        const int row = (lane >> 3) + 4 * j;
+        src[j] = (row < nrows) ? a.hidden + (size_t)a.row_token[r0 + row] * kHidden + (lane & 7) * 16 : a.hidden;
+      }
+      const int wrow1 = e * kGemm1N + 64 * g;
+      const int wrow2 = wrow1 + kInter;
+      for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutProducer);
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], kA1Bytes);
+          tma_load_2d(sA + stage * kA1Bytes, &a.tm_w1, &full[stage], kb * kBlk, wrow1, pol_w);
+          tma_load_2d(sA + stage * kA1Bytes + 64 * 128, &a.tm_w1, &full[stage], kb * kBlk, wrow2, pol_w);
+        }
+        last_parity[stage] = phase;
+        const uint32_t bdst = smem_u32(sB + stage * kB1Bytes);
+#pragma unroll
+        for (int j = 0; j < kRowsPerLane; ++j) {
+          const int row = (lane >> 3) + 4 * j;
+          cp_async_16(bdst + sw128_offset(row, lane & 7), src[j] + kb * kBlk, row < nrows ? 16u : 0u);
+        }
+        cp_async_commit();
+        ++issued;
+        if (issued > kLag) {
+          cp_async_wait_group<kLag>();
+          fence_proxy_async_smem();
+          __syncwarp();
+          int ps = stage - kLag;
+          if (ps < 0) ps += S;
+          if (lane == 0) mbar_arrive(&full[ps]);
+        }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // complete the last kLag stages (or fewer)
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const long tail = issued < kLag ? issued : kLag;
+      for (long i = tail; i >= 1; --i) {
+        int ps = stage - (int)i;
+        while (ps < 0) ps += S;
+        mbar_arrive(&full[ps]);
+      }
+      // drain: every issued TMA load must have landed before the smem is reused
+      for (int s = 0; s < S; ++s)
+        if (last_parity[s] != 0xFFFFFFFFu)
+          if (!mbar_wait(&full[s], last_parity[s], sAbort, kWaitBudgetNs) && !*sAbort) fail(kStatusTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(0u, 128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t kbg = 0;
+      bool ok = true;
+      bool any = false;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        for (int l = 0; l < nk; ++l) {
+          const uint32_t buf = kbg % kBufs1;
+          if (!mbar_wait(&tempty[buf], ((kbg / kBufs1) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
+              !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * kA1Bytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * kB1Bytes));
+          const uint32_t d = tmem_base + buf * BN;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mma_f8f6f4(d, adesc + 2 * j, bdesc + 2 * j, idesc, j > 0 ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          tc_commit(&tfull[buf]);
+          any = true;
+          ++kbg;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (any) {
+        // all issued MMAs complete before TMEM and shared memory are reused
+        tc_commit(drain);
+        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    constexpr int G = kSets;
+    const int set = (warp - 4) >> 2;   // this warp's K-block residue class
+    const int ew = warp & 3;           // TMEM lane quarter
+    const int row = ew * 32 + lane;    // A row == TMEM lane
+    const int etid = threadIdx.x - 128;
+    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+    uint32_t kbg = 0;                  // K-blocks this CTA processed before the current item
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int u = it / n_split, sp = it % n_split;
+      const int4 blk = a.blocks[u / kG1Slices];
+      const int g = u % kG1Slices;
+      const int e = blk.x, r0 = blk.y, nrows = blk.z;
+      if (etid < BN) sTok[etid] = (etid < nrows) ? a.row_token[r0 + etid] : -1;
+      if (etid < 2 * kHBlocks) {
+        const int h = etid / kHBlocks, kb = etid % kHBlocks;
+        const int nbk = h * (kInter / kBlk) + g / 2;
+        sWScale[etid] = a.w1_scale[((size_t)e * (kGemm1N / kBlk) + nbk) * kHBlocks + kb];
+      }
+      named_barrier_sync(1, kEpi1Threads);
+      for (int i = etid; i < kHBlocks * BN; i += kEpi1Threads) {
+        const int kb = i / BN, t = i % BN;
+        const int tok = sTok[t];
+        sAScale[i] = tok >= 0 ? a.hidden_scale[(size_t)kb * a.T + tok] : 0.0f;
+      }
+      named_barrier_sync(1, kEpi1Threads);
+
+      float acc[BN];
+#pragma unroll
+      for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
+      const float* wsc = sWScale + (ew < 2 ? 0 : kHBlocks);
+      bool bad = false;
+      // this set takes the item's K-blocks whose CTA-wide index is = set (mod G)
+      for (int l = (set - (int)(kbg % G) + G) % G; l < nk; l += G) {
+        const uint32_t kgl = kbg + l;
+        const uint32_t buf = kgl % kBufs1;
+        if (!mbar_wait(&tfull[buf], (kgl / kBufs1) & 1u, sAbort, kWaitBudgetNs)) {
+          bad = true;
+          if (lane == 0) fail(kStatusTimeoutEpilogue);
+          break;
+        }
+        tc_fence_after();
+        const int kb = sp * nk + l;
+        const float ws = wsc[kb];
+        const float* asc = sAScale + kb * BN;
+        float p[16];
+        tmem_ld16(tmem_base + lane_base + buf * BN, p);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(p[i], ws * asc[i], acc[i]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+      }
+      kbg += nk;
+      // Each set publishes its partial sums; they are added in set order.
+      if (!bad) {
+        float* mine = sXch + (size_t)(set * 128 + row) * kXchStride;
+#pragma unroll
+        for (int t = 0; t < BN; ++t) mine[t] = acc[t];
+      }
+      if (named_barrier_or(1, kEpi1Threads, bad)) {
+        ok = false;
+        break;
+      }
+      bool last = true;
+      if (n_split > 1) {
+        // publish this item's partial, then find out whether it completes the unit
+        float* part = a.split_part + (size_t)it * 128 * BN;
+        for (int i = etid; i < 128 * BN; i += kEpi1Threads) {
+          const int r = i / BN, t = i % BN;
+          float v = 0.0f;
+#pragma unroll
+          for (int j = 0; j < G; ++j) v += sXch[(size_t)(j * 128 + r) * kXchStride + t];
+          part[i] = v;
+        }
+        __threadfence();
+        named_barrier_sync(1, kEpi1Threads);
+        if (etid == 0) *sLast = (atomicAdd(&a.split_count[u], 1) == n_split - 1) ? 1 : 0;
+        named_barrier_sync(1, kEpi1Threads);
+        last = *sLast != 0;
+        if (last) __threadfence();
+      }
+      if (last) {
+        // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).
+        const float* parts = a.split_part + (size_t)u * n_split * 128 * BN;
+        for (int i = etid; i < 64 * BN; i += kEpi1Threads) {
+          const int r = i % 64, t = i / 64;
+          if (t < nrows) {
+            float x1 = 0.0f, x2 = 0.0f;
+            if (n_split == 1) {
+#pragma unroll
+              for (int j = 0; j < G; ++j) {
+                x1 += sXch[(size_t)(j * 128 + r) * kXchStride + t];
+                x2 += sXch[(size_t)(j * 128 + 64 + r) * kXchStride + t];
+              }
+            } else {
+              for (int q = 0; q < n_split; ++q) {
+                x1 += __ldcg(parts + (size_t)q * 128 * BN + r * BN + t);
+                x2 += __ldcg(parts + (size_t)q * 128 * BN + (64 + r) * BN + t);
+              }
+            }
+            bool sat = false;
+            const float silu = x2 / (1.0f + expf(-x2));
+            a.inter[(size_t)(r0 + t) * kInter + 64 * g + r] = to_half_sat(silu * x1, sat);
+            if (sat) atomicOr(a.status, kStatusSaturated);
+          }
+        }
+        if (n_split > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
+        __threadfence();  // the slice's rows are visible before the block counter moves
+      }
+      named_barrier_sync(1, kEpi1Threads);
+      // one more of this block's 32 slices is published (GEMM2 waits for all 32)
+      if (last && etid == 0) atomicAdd(&a.blk_ready[u / kG1Slices], 1);
+    }
+  }
+}
+
+// ============================================================== GEMM2 phase
+__device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
+                                            int nb, volatile int* sAbort, volatile int* sCombine) {
+  constexpr int SR = kRawStages, SC = kConvStages, SB = kBStages;
+  uint8_t* sRaw = sm + kP2Raw;
+  uint8_t* sAh = sm + kP2Ah;
+  uint8_t* sB = sm + kP2B;
+  uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
+  uint64_t* raw_empty = bars + SR;             // converters done reading it
+  uint64_t* a_full = bars + 2 * SR;            // f16 W2 tile written by the converters
+  uint64_t* c_empty = bars + 2 * SR + SC;      // MMA done with the converted slot
+  uint64_t* b_full = bars + 2 * SR + 2 * SC;   // intermediate rows landed (TMA)
+  uint64_t* b_empty = b_full + SB;             // MMA done with the intermediate slot
+  uint64_t* tfull = b_empty + SB;
+  uint64_t* tempty = tfull + kBufs2;
+  uint64_t* drain = tempty + kBufs2;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_units = nb * kG2Slices;
+  const int n_split = a.splits[1];               // K splits per unit
+  const int nk = kIBlocks / n_split;             // K-blocks per work item
+  const int n_items = n_units * n_split;
+  auto fail = [&](uint32_t bit) {
+    *sAbort = 1;
+    atomicOr(a.status, bit);
+  };
+
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ producers
+    if (lane == 0) {
+      const bool w2_side = (warp == 0);
+      const uint64_t pol = w2_side ? l2_policy_evict_first() : l2_policy_evict_last();
+      const int n = w2_side ? SR : SB;
+      uint64_t* fullb = w2_side ? raw_full : b_full;
+      uint64_t* emptyb = w2_side ? raw_empty : b_empty;
+      Ring ring(n);
+      bool ok = true;
+      int ready_blk = -1;  // block whose intermediate rows are known complete
+      uint32_t last_parity[SR > SB ? SR : SB];
+      for (int s = 0; s < n; ++s) last_parity[s] = 0xFFFFFFFFu;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const int u = it / n_split, sp = it % n_split;
+        const int b = u / kG2Slices;
+        const int4 blk = a.blocks[b];
+        const int h = u % kG2Slices;
+        const int e = blk.x, r0 = blk.y;
+        if (!w2_side && b != ready_blk) {
+          // wait until GEMM1 published all 32 slices of this block's rows
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
+            if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
+              ok = false;
+              fail(kStatusTimeoutProducer);
+              break;
+            }
+            __nanosleep(200);
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
+          ready_blk = b;
+        }
+        for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
+          if (!mbar_wait(&emptyb[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutProducer);
+            break;
+          }
+          if (w2_side) {
+            mbar_arrive_expect_tx(&fullb[ring.slot], kRawBytes);
+            tma_load_2d(sRaw + ring.slot * kRawBytes, &a.tm_w2, &fullb[ring.slot], kb * kBlk, e * kHidden + h * 128,
+                        pol);
+          } else {
+            uint8_t* bb = sB + ring.slot * kB2Bytes;
+            mbar_arrive_expect_tx(&fullb[ring.slot], kB2Bytes);
+            tma_load_2d(bb, &a.tm_inter, &fullb[ring.slot], kb * kBlk, r0, pol);
+            tma_load_2d(bb + BN * 128, &a.tm_inter, &fullb[ring.slot], kb * kBlk + 64, r0, pol);
+          }
+          last_parity[ring.slot] = ring.phase;
+          ring.next();
+        }
+      }
+      // every issued TMA load lands before the CTA exits
+      for (int s = 0; s < n; ++s)
+        if (last_parity[s] != 0xFFFFFFFFu)
+          if (!mbar_wait(&fullb[s], last_parity[s], sAbort, kWaitBudgetNs) && !*sAbort) fail(kStatusTimeoutDrain);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(0u, 128, BN);  // f16 x f16
+      Ring ring(SC), bring(SB);
+      uint32_t ug = 0;
+      bool ok = true;
+      bool any = false;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ug) {
+        const uint32_t buf = ug % kBufs2;
+        if (!mbar_wait(&tempty[buf], ((ug / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          fail(kStatusTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs) ||
+              !mbar_wait(&b_full[bring.slot], bring.phase, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const uint64_t adesc = umma_desc_sw128(smem_u32(sAh + ring.slot * kAhBytes + half * 128 * 128));
+            const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + bring.slot * kB2Bytes + half * BN * 128));
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              mma_f16(d, adesc + 2 * j, bdesc + 2 * j, idesc, (kb | half | j) ? 1u : 0u);
+          }
+          tc_commit(&c_empty[ring.slot]);
+          tc_commit(&b_empty[bring.slot]);
+          any = true;
+          ring.next();
+          bring.next();
+        }
+        if (!ok) break;
+        tc_commit(&tfull[buf]);
+      }
+      if (any) {
+        tc_commit(drain);
+        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+      }
+    }
+    __syncwarp();
+  } else if ((warp >= 4 && warp < 8) || (warp >= 12 && warp < 16)) {
+    // ------------------------------------------------------------ converters
+    // 8 warps; thread c converts 16-byte chunks c, c + 256, c + 512, c + 768 of the
+    // raw tile (row = chunk / 8, K bytes 16 * (chunk % 8)): one HMUL2 per 2 weights.
+    const int ctid = (warp < 8 ? warp - 4 : warp - 8) * 32 + lane;  // 0..255
+    Ring rr(SR), cr(SC);
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int u = it / n_split, sp = it % n_split;
+      const int4 blk = a.blocks[u / kG2Slices];
+      const int h = u % kG2Slices;
+      const float* sc = a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
+      const int kexp = w2_block_exponent(sc);
+      // the unit's 16 scales, one per lane: no global load on the per-stage path
+      const float lane_scale = __ldg(sc + (lane & (kIBlocks - 1)));
+      for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
+        if (!mbar_wait(&raw_full[rr.slot], rr.phase, sAbort, kWaitBudgetNs) ||
+            !mbar_wait(&c_empty[cr.slot], cr.phase ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutConvert);
+          break;
+        }
+        const __half2 sc2 = __half2half2(__float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, kb), kexp)));
+        const uint8_t* raw = sRaw + rr.slot * kRawBytes;
+        uint8_t* ah = sAh + cr.slot * kAhBytes;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = ctid + 256 * i;
+          const int r = c >> 3, cc = c & 7;
+          const uint4 q = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, cc));
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+          uint32_t o[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] & 0xFFFFu), __NV_E4M3);
+            const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] >> 16), __NV_E4M3);
+            const __half2 pl = __hmul2(*reinterpret_cast<const __half2*>(&lo), sc2);
+            const __half2 ph = __hmul2(*reinterpret_cast<const __half2*>(&hi), sc2);
+            o[2 * j] = *reinterpret_cast<const uint32_t*>(&pl);
+            o[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&ph);
+          }
+          uint8_t* dst = ah + (cc >> 2) * (128 * 128);
+          const int c2 = (cc & 3) * 2;
+          *reinterpret_cast<uint4*>(dst + sw128_offset(r, c2)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(dst + sw128_offset(r, c2 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&raw_empty[rr.slot]);
+          mbar_arrive(&a_full[cr.slot]);
+        }
+        rr.next();
+        cr.next();
+      }
+    }
+  } else if (warp >= 8 && warp < 12) {
+    // ------------------------------------------------------------ epilogue + combine
+    const int ew = warp - 8;
+    const int etid = threadIdx.x - 256;  // 0..127
+    const int hrow = ew * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+    const int slice_items = nb * n_split;  // items that write pair rows of one hidden slice
+    uint32_t ug = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ug) {
+      const int u = it / n_split, sp = it % n_split;
+      const int4 blk = a.blocks[u / kG2Slices];
+      const int h = u % kG2Slices;
+      const int r0 = blk.y, nrows = blk.z;
+      const uint32_t buf = ug % kBufs2;
+      const bool bad = !mbar_wait(&tfull[buf], (ug / kBufs2) & 1u, sAbort, kWaitBudgetNs);
+      if (bad) {
+        if (lane == 0) fail(kStatusTimeoutEpilogue);
+      } else {
+        tc_fence_after();
+        __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
+        const float* wrow = a.row_weight + r0;
+        // the converters scaled W2 by 2^k (see w2_block_exponent): undo it exactly
+        const int kexp = w2_block_exponent(a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks);
+        bool sat = false;
+        float p[16];
+        tmem_ld16(tmem_base + lane_base + buf * BN, p);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < nrows) dst[(size_t)i * kHidden] = to_half_sat(p[i] * ldexpf(__ldg(wrow + i), -kexp), sat);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        if (sat) atomicOr(a.status, kStatusSaturated);
+        __threadfence();  // this item's pair rows are visible before the slice counter moves
+      }
+      // all four warps arrive here every item (no early exit before the barrier)
+      if (named_barrier_or(2, 128, bad)) {
+        ok = false;
+        break;
+      }
+      if (etid == 0) *sCombine = (atomicAdd(&a.slice_cnt[h], 1) == slice_items - 1) ? 1 : 0;
+      named_barrier_sync(2, 128);
+      if (*sCombine) {
+        // Last item of hidden slice h: out[t, 128h .. 128h+127] for every token,
+        // summing the token's pair rows over planes, then slots, in fixed order.
+        __threadfence();
+        const int planes = n_split;
+        const int cg = etid & 15;  // 8-column group
+        for (int t = etid >> 4; t < a.T; t += 8) {
+          float acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+          const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
+          const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
+          const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+          const size_t col = (size_t)h * 128 + cg * 8;
+          for (int s = 0; s < planes; ++s)
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+              if (rows[k] >= 0) {
+                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)s * a.plane_elems +
+                                                                      (size_t)rows[k] * kHidden + col));
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                  acc[2 * i] += f.x;
+                  acc[2 * i + 1] += f.y;
+                }
+              }
+            }
+          if (a.f32_out) {
+            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + (size_t)t * kHidden + col);
+            o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+          } else {
+            uint4 o;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const __nv_bfloat162 bv = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+              ow[i] = *reinterpret_cast<const uint32_t*>(&bv);
+            }
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)t * kHidden + col) = o;
+          }
+        }
+        if (etid == 0) a.slice_cnt[h] = 0;  // ready for the next call
+      }
+      named_barrier_sync(2, 128);  // sCombine is rewritten by the next item
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars1 = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint64_t* bars2 = bars1 + kNumBars1;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sm + kOffMisc + 4);
+  volatile int* sLast = reinterpret_cast<volatile int*>(sm + kOffMisc + 8);
+  volatile int* sCombine = reinterpret_cast<volatile int*>(sm + kOffMisc + 12);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    // phase 1: full/empty [8], tfull/tempty [32], drain
+    for (int s = 0; s < kStages1; ++s) {
+      mbar_init(&bars1[s], 2);               // producer expect_tx arrive + cp.async completion arrive
+      mbar_init(&bars1[kStages1 + s], 1);    // tcgen05.commit
+    }
+    for (int b = 0; b < kBufs1; ++b) {
+      mbar_init(&bars1[2 * kStages1 + b], 1);           // tcgen05.commit
+      mbar_init(&bars1[2 * kStages1 + kBufs1 + b], 4);  // one arrive per warp of the owning set
+    }
+    mbar_init(&bars1[2 * kStages1 + 2 * kBufs1], 1);
+    // phase 2: raw full/empty, converted full/empty, intermediate full/empty, tfull/tempty, drain
+    uint64_t* b2 = bars2;
+    for (int s = 0; s < kRawStages; ++s) {
+      mbar_init(&b2[s], 1);
+      mbar_init(&b2[kRawStages + s], 8);  // one arrive per converter warp
+    }
+    b2 += 2 * kRawStages;
+    for (int s = 0; s < kConvStages; ++s) {
+      mbar_init(&b2[s], 8);
+      mbar_init(&b2[kConvStages + s], 1);
+    }
+    b2 += 2 * kConvStages;
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&b2[s], 1);
+      mbar_init(&b2[kBStages + s], 1);
+    }
+    b2 += 2 * kBStages;
+    for (int b = 0; b < kBufs2; ++b) {
+      mbar_init(&b2[b], 1);
+      mbar_init(&b2[kBufs2 + b], 4);
+    }
+    mbar_init(&b2[2 * kBufs2], 1);
+    *sAbort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&a.tm_w1);
+    tma_prefetch_desc(&a.tm_w2);
+    tma_prefetch_desc(&a.tm_inter);
+  }
+  if (warp == 1) {
+    tmem_alloc(sTmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
+  fence_proxy_async_global();
+  const uint32_t tmem_base = *sTmem;
+  const int nb = *a.n_blocks;
+
+  if (nb == 0) {
+    // no local (token, expert) pair: the output is all zeros
+    const size_t n16 = (size_t)a.T * kHidden * (a.f32_out ? 4 : 2) / 16;
+    uint4* o = reinterpret_cast<uint4*>(a.out);
+    for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n16; i += (size_t)gridDim.x * kThreads)
+      o[i] = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    gemm1_phase(a, sm, bars1, tmem_base, nb, sAbort, sLast);
+    // The shared region changes role: order this CTA's generic-proxy accesses of
+    // phase 1 before the TMA writes of phase 2, and phase 1's TMEM reads before
+    // phase 2's MMAs.
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (!*sAbort) gemm2_phase(a, sm, bars2, tmem_base, nb, sAbort, sCombine);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
+                          const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
+                          const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
+                          cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (err != cudaSuccess) return err;
+    attr_set[dev] = true;
+  }
+  DecodeArgs a;
+  a.tm_w1 = *tm_w1;
+  a.tm_w2 = *tm_w2;
+  a.tm_inter = *tm_inter;
+  a.hidden = hidden;
+  a.hidden_scale = hidden_scale;
+  a.w1_scale = w1_scale;
+  a.w2_scale = w2_scale;
+  a.n_blocks = reinterpret_cast<const int32_t*>(ws + L.n_blocks);
+  a.blocks = reinterpret_cast<const int4*>(ws + L.blocks);
+  a.row_token = reinterpret_cast<const int32_t*>(ws + L.row_token);
+  a.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
+  a.token_rows = reinterpret_cast<const int32_t*>(ws + L.token_rows);
+  a.splits = reinterpret_cast<const int32_t*>(ws + L.splits);
+  a.split_count = reinterpret_cast<int32_t*>(ws + L.split_count);
+  a.split_part = reinterpret_cast<float*>(ws + L.split_part);
+  a.blk_ready = reinterpret_cast<int32_t*>(ws + L.blk_ready);
+  a.slice_cnt = reinterpret_cast<int32_t*>(ws + L.slice_cnt);
+  a.inter = reinterpret_cast<__half*>(ws + L.inter);
+  a.pair_out = reinterpret_cast<__half*>(ws + L.pair_out);
+  a.out = out;
+  a.status = reinterpret_cast<uint32_t*>(ws + L.status);
+  a.plane_elems = (size_t)L.pcap * kHidden;
+  a.T = T;
+  a.f32_out = f32_out ? 1 : 0;
+  const int grid = num_sms > 0 ? num_sms : 1;
+  return launch_pdl(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, a);
+}
+
+}  // namespace fbmoe

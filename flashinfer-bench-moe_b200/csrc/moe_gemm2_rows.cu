@@ -65,18 +65,6 @@ struct Ring {
   }
 };
 
-// Exponent k with max(s) * 2^k in (32, 64] for the 16 scales of one 128-row block.
-__device__ __forceinline__ int block_exponent(const float* s16) {
-  float m = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kIBlocks; ++i) m = fmaxf(m, fabsf(__ldg(s16 + i)));
-  if (!(m > 0.0f) || !isfinite(m)) return 0;
-  int ex;
-  frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
-  int k = 6 - ex;  // m * 2^k in [32, 64)
-  return k < -60 ? -60 : (k > 60 ? 60 : k);
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_rows_kernel(const __grid_constant__ CUtensorMap tm_w2raw, const __grid_constant__ CUtensorMap tm_inter,
                       const float* __restrict__ w2_scale, const int32_t* __restrict__ n_blocks_ptr,
@@ -242,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nt = u % kNTiles;
       const float* s_lo = w2_scale + ((size_t)blk.x * kHBlocks + 2 * nt) * kIBlocks;  // rows 0..127
       const float* s_hi = s_lo + kIBlocks;                                           // rows 128..255
-      const int k_lo = block_exponent(s_lo), k_hi = block_exponent(s_hi);
+      const int k_lo = w2_block_exponent(s_lo), k_hi = w2_block_exponent(s_hi);
       // lanes 0-15 hold the first block's 16 scales, lanes 16-31 the second's
       const float lane_scale = __ldg((lane < 16 ? s_lo : s_hi) + (lane & 15));
       for (int ks = 0; ks < kKSteps; ++ks) {
@@ -299,8 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r0 = blk.y, nrows = blk.z;
       const float* s_lo = w2_scale + ((size_t)blk.x * kHBlocks + 2 * nt) * kIBlocks;
       const float wr = row < nrows ? __ldg(row_weight + r0 + row) : 0.0f;
-      const float f_lo = ldexpf(wr, -block_exponent(s_lo));
-      const float f_hi = ldexpf(wr, -block_exponent(s_lo + kIBlocks));
+      const float f_lo = ldexpf(wr, -w2_block_exponent(s_lo));
+      const float f_hi = ldexpf(wr, -w2_block_exponent(s_lo + kIBlocks));
       const uint32_t buf = ug & 1u;
       if (!mbar_wait(&tfull[buf], (ug >> 1) & 1u, sAbort, kWaitBudgetNs)) {
         ok = false;
