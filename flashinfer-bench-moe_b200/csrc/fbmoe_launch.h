@@ -45,7 +45,7 @@ struct Layout {
   size_t split_count;  // int32[kSplitItems]: arrivals per GEMM1 unit (split-K fix-up)
   size_t split_part;   // fp32[kSplitItems][128][16]: GEMM1 split partial sums
   size_t blk_ready;    // int32[max_blocks]: GEMM1 slices published per block (decode kernel)
-  size_t slice_cnt;    // int32[56]: GEMM2 items finished per hidden slice (decode kernel)
+  size_t grid_sync;    // int32[1]: CTAs of the decode kernel done with GEMM2 (zeroed by permute)
   size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
   size_t total;        // bytes
   int pcap;            // row capacity (multiple of 128)

@@ -68,7 +68,7 @@ Layout make_layout(int T, int E_local, bool allow_split) {
   L.split_count = take((size_t)L.split_items * 4);
   L.split_part = take((size_t)L.split_items * 128 * 16 * 4);
   L.blk_ready = take((size_t)L.max_blocks * 4);
-  L.slice_cnt = take((size_t)(kHidden / 128) * 4);
+  L.grid_sync = take(16);
   const bool big = bn == 128;
   L.chunk_cnt = take((tt + 1023) / 1024 * (size_t)el * 4);
   L.a_perm = take(big ? (size_t)pcap * kHidden : 0);

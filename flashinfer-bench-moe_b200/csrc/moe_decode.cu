@@ -22,11 +22,11 @@
 // W2 before the last GEMM1 CTA retired.  Here every CTA runs its GEMM1 work items,
 // then its GEMM2 items: W2 tiles stream in at once, and only the intermediate
 // rows of a block wait for that block's 32 GEMM1 slices (a per-block counter
-// that GEMM1 raises after publishing them).  The combine of hidden slice h runs
-// in the CTA whose GEMM2 item for slice h arrives last on the slice's counter,
-// so no grid-wide barrier exists.  The grid is at most one CTA per SM with one
-// CTA resident per SM, and nothing in GEMM1 waits on GEMM2, so every wait ends;
-// every wait is also bounded in wall time.
+// that GEMM1 raises after publishing them).  The combine runs after one grid-wide
+// arrival (every CTA has written its pair rows) and is spread over all threads.
+// The grid is at most one CTA per SM with one CTA resident per SM, nothing in
+// GEMM1 waits on GEMM2 and every CTA reaches the grid arrival, so every wait
+// ends; every wait is also bounded in wall time.
 //
 // Orientation (swap-AB) in both GEMMs: weight rows are the MMA's M = 128 operand
 // and the <= 16 token rows of a block its N operand.
@@ -51,7 +51,7 @@
 // operand).  Split-K: splits[1] = S > 1 shares a unit's 16 K-blocks among S items
 // that write separate planes of pair rows; the combine adds the planes.
 // Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 intermediate producer (TMA),
-// w4-w7 and w12-w15 converters, w8-w11 epilogue (+ combine), the rest idle.
+// w4-w7 and w12-w15 converters, w8-w11 epilogue, the rest idle; then all threads combine.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -71,7 +71,9 @@ constexpr int kEpi1Threads = 128 * kSets;
 // (two split-K items) ahead of the promotion epilogue, whose per-item fix-up
 // (partials to L2, fence, counter) would otherwise stall the weight stream.
 constexpr int kBufs1 = 32;
-constexpr int kStages1 = 8;
+// 10 stages = 160 KB of W1 in flight per SM: HBM streaming at ~2 us loaded latency
+// needs roughly 90 KB per SM, and more absorbs the latency spread.
+constexpr int kStages1 = 10;
 // A stage's cp.async row copies are signalled complete kLag stages after they
 // are issued, so up to kLag stages of row copies are in flight.
 constexpr int kLag = kStages1 - 2;
@@ -86,8 +88,10 @@ constexpr int kP1Xch = kP1WScale + 2 * kHBlocks * 4;
 constexpr int kP1Tok = kP1Xch + kSets * 128 * kXchStride * 4;
 constexpr int kP1End = kP1Tok + BN * 4;
 // ---- GEMM2 phase layout
-constexpr int kRawStages = 4;
-constexpr int kConvStages = 3;
+// 8 raw W2 stages (128 KB in flight per SM) and 2 converted stages: the raw ring
+// is what streams from HBM; the converters run at shared-memory speed.
+constexpr int kRawStages = 8;
+constexpr int kConvStages = 2;
 constexpr int kBStages = 6;
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kAhBytes = 2 * 128 * 128;     // f16 W2 tile (two 64-K halves)
@@ -130,7 +134,7 @@ struct DecodeArgs {
   int32_t* split_count;
   float* split_part;
   int32_t* blk_ready;
-  int32_t* slice_cnt;
+  int32_t* grid_sync;
   __half* inter;
   __half* pair_out;
   void* out;
@@ -424,7 +428,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 
 // ============================================================== GEMM2 phase
 __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
-                                            int nb, volatile int* sAbort, volatile int* sCombine) {
+                                            int nb, volatile int* sAbort) {
   constexpr int SR = kRawStages, SC = kConvStages, SB = kBStages;
   uint8_t* sRaw = sm + kP2Raw;
   uint8_t* sAh = sm + kP2Ah;
@@ -614,96 +618,109 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       }
     }
   } else if (warp >= 8 && warp < 12) {
-    // ------------------------------------------------------------ epilogue + combine
+    // ------------------------------------------------------------ epilogue
     const int ew = warp - 8;
-    const int etid = threadIdx.x - 256;  // 0..127
     const int hrow = ew * 32 + lane;
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    const int slice_items = nb * n_split;  // items that write pair rows of one hidden slice
     uint32_t ug = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ug) {
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++ug) {
       const int u = it / n_split, sp = it % n_split;
       const int4 blk = a.blocks[u / kG2Slices];
       const int h = u % kG2Slices;
       const int r0 = blk.y, nrows = blk.z;
       const uint32_t buf = ug % kBufs2;
-      const bool bad = !mbar_wait(&tfull[buf], (ug / kBufs2) & 1u, sAbort, kWaitBudgetNs);
-      if (bad) {
+      if (!mbar_wait(&tfull[buf], (ug / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
         if (lane == 0) fail(kStatusTimeoutEpilogue);
-      } else {
-        tc_fence_after();
-        __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
-        const float* wrow = a.row_weight + r0;
-        // the converters scaled W2 by 2^k (see w2_block_exponent): undo it exactly
-        const int kexp = w2_block_exponent(a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks);
-        bool sat = false;
-        float p[16];
-        tmem_ld16(tmem_base + lane_base + buf * BN, p);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (i < nrows) dst[(size_t)i * kHidden] = to_half_sat(p[i] * ldexpf(__ldg(wrow + i), -kexp), sat);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
-        if (sat) atomicOr(a.status, kStatusSaturated);
-        __threadfence();  // this item's pair rows are visible before the slice counter moves
-      }
-      // all four warps arrive here every item (no early exit before the barrier)
-      if (named_barrier_or(2, 128, bad)) {
-        ok = false;
         break;
       }
-      if (etid == 0) *sCombine = (atomicAdd(&a.slice_cnt[h], 1) == slice_items - 1) ? 1 : 0;
-      named_barrier_sync(2, 128);
-      if (*sCombine) {
-        // Last item of hidden slice h: out[t, 128h .. 128h+127] for every token,
-        // summing the token's pair rows over planes, then slots, in fixed order.
-        __threadfence();
-        const int planes = n_split;
-        const int cg = etid & 15;  // 8-column group
-        for (int t = etid >> 4; t < a.T; t += 8) {
-          float acc[8];
+      tc_fence_after();
+      __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
+      const float* wrow = a.row_weight + r0;
+      // the converters scaled W2 by 2^k (see w2_block_exponent): undo it exactly
+      const int kexp = w2_block_exponent(a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks);
+      bool sat = false;
+      float p[16];
+      tmem_ld16(tmem_base + lane_base + buf * BN, p);
+      tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-          const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
-          const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
-          const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
-          const size_t col = (size_t)h * 128 + cg * 8;
-          for (int s = 0; s < planes; ++s)
+      for (int i = 0; i < 16; ++i)
+        if (i < nrows) dst[(size_t)i * kHidden] = to_half_sat(p[i] * ldexpf(__ldg(wrow + i), -kexp), sat);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (sat) atomicOr(a.status, kStatusSaturated);
+    }
+  }
+}
+
+// ============================================================== combine phase
+// After every CTA has written its pair rows (one arrival each on a grid counter
+// that the permute kernel zeroed): out[t, 8c .. 8c+7] for every token t and
+// column group c, spread over all threads of the grid.  The token's pair rows are
+// summed over planes, then slots, in fixed order (deterministic), in fp32.
+__device__ __forceinline__ void combine_phase(const DecodeArgs& a, volatile int* sAbort) {
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
+    atomicAdd(a.grid_sync, 1);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu(a.grid_sync) < (int)gridDim.x) {
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        *sAbort = 1;
+        atomicOr(a.status, kStatusTimeoutEpilogue);
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+  __syncthreads();
+  if (*sAbort) return;
+  const int planes = a.splits[1];
+  constexpr int kGroupsPerRow = kHidden / 8;
+  const int tasks = a.T * kGroupsPerRow;
+  // consecutive tasks go to different CTAs, so a small T still uses many SMs
+  for (int task = threadIdx.x * gridDim.x + blockIdx.x; task < tasks; task += gridDim.x * kThreads) {
+    const int t = task / kGroupsPerRow;
+    const size_t col = (size_t)(task % kGroupsPerRow) * 8;
+    float acc[8];
 #pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-              if (rows[k] >= 0) {
-                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)s * a.plane_elems +
-                                                                      (size_t)rows[k] * kHidden + col));
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
+    const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
+    const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+    for (int s = 0; s < planes; ++s) {
+      // the plane's (up to 8) rows are loaded together: one L2 round trip per plane
+      uint4 v[kTopK];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-                  acc[2 * i] += f.x;
-                  acc[2 * i + 1] += f.y;
-                }
-              }
-            }
-          if (a.f32_out) {
-            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + (size_t)t * kHidden + col);
-            o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-          } else {
-            uint4 o;
-            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+      for (int k = 0; k < kTopK; ++k)
+        v[k] = rows[k] >= 0 ? __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)s * a.plane_elems +
+                                                                    (size_t)rows[k] * kHidden + col))
+                            : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const __nv_bfloat162 bv = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-              ow[i] = *reinterpret_cast<const uint32_t*>(&bv);
-            }
-            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)t * kHidden + col) = o;
+      for (int k = 0; k < kTopK; ++k) {
+        if (rows[k] >= 0) {
+          const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
           }
         }
-        if (etid == 0) a.slice_cnt[h] = 0;  // ready for the next call
       }
-      named_barrier_sync(2, 128);  // sCombine is rewritten by the next item
+    }
+    if (a.f32_out) {
+      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + (size_t)t * kHidden + col);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 bv = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        ow[i] = *reinterpret_cast<const uint32_t*>(&bv);
+      }
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)t * kHidden + col) = o;
     }
   }
 }
@@ -716,7 +733,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + kOffMisc);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sm + kOffMisc + 4);
   volatile int* sLast = reinterpret_cast<volatile int*>(sm + kOffMisc + 8);
-  volatile int* sCombine = reinterpret_cast<volatile int*>(sm + kOffMisc + 12);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -789,7 +805,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (!*sAbort) gemm2_phase(a, sm, bars2, tmem_base, nb, sAbort, sCombine);
+    if (!*sAbort) gemm2_phase(a, sm, bars2, tmem_base, nb, sAbort);
+    __syncthreads();  // this CTA's pair rows are all written
+    combine_phase(a, sAbort);
   }
 
   tc_fence_before();
@@ -831,7 +849,7 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.split_count = reinterpret_cast<int32_t*>(ws + L.split_count);
   a.split_part = reinterpret_cast<float*>(ws + L.split_part);
   a.blk_ready = reinterpret_cast<int32_t*>(ws + L.blk_ready);
-  a.slice_cnt = reinterpret_cast<int32_t*>(ws + L.slice_cnt);
+  a.grid_sync = reinterpret_cast<int32_t*>(ws + L.grid_sync);
   a.inter = reinterpret_cast<__half*>(ws + L.inter);
   a.pair_out = reinterpret_cast<__half*>(ws + L.pair_out);
   a.out = out;

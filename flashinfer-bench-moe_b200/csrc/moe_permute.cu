@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
                                                           int32_t* __restrict__ split_count, int split_items,
                                                           int pair_planes, const int32_t* __restrict__ chunk_cnt,
                                                           int n_chunks, int32_t* __restrict__ blk_ready,
-                                                          int32_t* __restrict__ slice_cnt) {
+                                                          int32_t* __restrict__ grid_sync) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   PermuteSmem& S = *reinterpret_cast<PermuteSmem*>(smem_raw);
   const int tid = threadIdx.x;
@@ -210,9 +210,9 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
       const int units = S.n_blocks * (kInter / 64);
       for (int i = tid; i < units; i += kThreads) split_count[i] = 0;
     }
-    // the decode kernel's per-block and per-slice arrival counters
+    // the decode kernel's per-block and grid arrival counters
     for (int i = tid; i < S.n_blocks; i += kThreads) blk_ready[i] = 0;
-    if (tid < kHidden / 128) slice_cnt[tid] = 0;
+    if (tid == 0) grid_sync[0] = 0;
   }
 
   // Phase C: deterministic scatter of this chunk.
@@ -286,7 +286,7 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
       reinterpret_cast<uint32_t*>(ws + L.status), num_sms, reinterpret_cast<int32_t*>(ws + L.splits),
       reinterpret_cast<int32_t*>(ws + L.split_count), L.split_items, L.pair_planes,
       static_cast<const int32_t*>(chunk_cnt), n_chunks, reinterpret_cast<int32_t*>(ws + L.blk_ready),
-      reinterpret_cast<int32_t*>(ws + L.slice_cnt));
+      reinterpret_cast<int32_t*>(ws + L.grid_sync));
 }
 
 }  // namespace fbmoe
