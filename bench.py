@@ -254,7 +254,8 @@ def run_ours(args, world, rank, local):
         "config": {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
                    "parallelism": f"ep{world}", "combine": "none" if world == 1 else "nccl reduce_scatter fp32",
                    "l2": "inputs larger than L2 (weights %.1f GB per GPU)" % (E_local * BYTES_PER_EXPERT / 1e9)},
-        "roofline": roofline, "e2e": e2e, "gpu_launches": 5 * args.steps, "clocks": clk.summary(),
+        "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_forward(T_EP, E_local) * args.steps,
+        "clocks": clk.summary(),
     }
     if world == 1 and not args.no_sweep:
         line["decode_sweep"] = decode_sweep(peaks)
@@ -306,6 +307,15 @@ def run_e2e(args, world, rank, inp, E_local, off):
     ms = max_over_ranks(s.elapsed_time(e), world)
     return {"value": round(T_EP * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms / n, 4)}
+
+
+def launches_per_forward(T, E_local):
+    """Our kernels per forward (mirrors forward_core in csrc/moe_capi.cu): T <= 64: router, permute, decode
+    kernel; otherwise router, [per-chunk count], permute, gather, GEMM1, GEMM2, combine."""
+    import fbmoe_lib as L
+    if L.block_rows(T, E_local) == 16:
+        return 3
+    return 6 + (1 if T > 1024 else 0)
 
 
 def flush_l2(buf):
@@ -463,7 +473,7 @@ def run_case(args):
     torch.cuda.set_device(0)
     peaks = load_peaks()
     weights = W.make_weights(32, 4242, "cuda")
-    inp = W.make_inputs(args.T, seed=args.T, config="standard" if args.case == "decode" else "skew",
+    inp = W.make_inputs(args.T, seed=args.T, config="skew" if args.case == "prefill" else "standard",
                         device="cuda", weights=weights)
     fargs = W.as_args(inp)
     buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
@@ -496,8 +506,9 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for cpu_baseline")
-    ap.add_argument("--case", choices=("ep", "decode", "prefill"), default="ep",
-                    help="ep = the benchmark line (default); decode/prefill = one small config for profiling")
+    ap.add_argument("--case", choices=("ep", "decode", "prefill", "shard"), default="ep",
+                    help="ep = the benchmark line (default); decode/prefill/shard = one small config for profiling "
+                         "(shard = uniform routing over 32 local experts: one rank's work at N=8 when T=8192)")
     ap.add_argument("--T", type=int, default=64, help="tokens for --case decode/prefill")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -97,8 +97,7 @@ constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kAhBytes = 2 * 128 * 128;     // f16 W2 tile (two 64-K halves)
 constexpr int kB2Bytes = BN * 256;          // f16 intermediate rows (two 64-K halves)
 // TMEM accumulators of GEMM2 items: 32 x 16 columns, so the MMA runs up to 32
-// items ahead of the epilogue (which publishes every item to L2 with a fence
-// and a counter before the next).
+// items ahead of the epilogue.
 constexpr int kBufs2 = 32;
 constexpr int kP2Raw = 0;
 constexpr int kP2Ah = kP2Raw + kRawStages * kRawBytes;
