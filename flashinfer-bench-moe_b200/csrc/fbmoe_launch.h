@@ -42,8 +42,8 @@ struct Layout {
   size_t chunk_cnt;    // int32[ceil(T/1024) * E_local] per-chunk expert counts (multi-CTA permute)
   size_t a_perm;       // e4m3[pcap * 7168]  token rows in permuted order (128-row blocks only)
   size_t splits;       // int32[2]: K splits of GEMM1 / GEMM2, chosen on the device per call
-  size_t split_count;  // int32[kSplitItems]: arrivals per GEMM1 unit (split-K fix-up)
-  size_t split_part;   // fp32[kSplitItems][128][16]: GEMM1 split partial sums
+  size_t split_count;  // int32[max_blocks * 32]: arrivals per GEMM1 unit (stream-K fix-up)
+  size_t split_part;   // fp32[kSplitItems][128][16]: GEMM1 partial sums, 2 slots per CTA
   size_t blk_ready;    // int32[max_blocks]: GEMM1 slices published per block (decode kernel)
   size_t grid_sync;    // int32[1]: CTAs of the decode kernel done with GEMM2 (zeroed by permute)
   size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
@@ -58,9 +58,9 @@ struct Layout {
 // allow_split: reserve the split-K buffers used for 16-row (decode) blocks.
 Layout make_layout(int T, int E_local, bool allow_split = true);
 
-// Split-K of the decode GEMMs: at most kSplitItems (unit, split) partials.
+// Decode stream-K: capacity of fp32 partial slots (two per CTA of the decode kernel).
 constexpr int kSplitItems = 1024;
-constexpr int kMaxPairPlanes = 4;
+constexpr int kMaxPairPlanes = 2;  // decode GEMM2 stream-K: at most 2 segments per unit
 int choose_block_rows(int T, int E_local);
 
 // Copies each routed token's row (and its 56 scales, [K-block][row]) to its
@@ -73,7 +73,7 @@ cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, floa
                          float* topk_w, uint32_t* status, cudaStream_t stream);
 
 // Histogram / padded offsets / deterministic permutation / GEMM block list.
-// Also picks the K splits of the GEMMs for num_sms CTAs (see moe_permute.cu).
+// Also zeroes the decode kernel's arrival counters.
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
                            int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream);
 

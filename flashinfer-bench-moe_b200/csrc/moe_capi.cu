@@ -65,7 +65,8 @@ Layout make_layout(int T, int E_local, bool allow_split) {
   L.split_items = split ? kSplitItems : 0;
   L.pair_out = take((size_t)pcap * kHidden * 2 * L.pair_planes);
   L.splits = take(16);
-  L.split_count = take((size_t)L.split_items * 4);
+  // one arrival counter per GEMM1 unit (32 per block), for the decode kernel's stream-K fix-up
+  L.split_count = take(split ? (size_t)L.max_blocks * (kInter / 64) * 4 : 0);
   L.split_part = take((size_t)L.split_items * 128 * 16 * 4);
   L.blk_ready = take((size_t)L.max_blocks * 4);
   L.grid_sync = take(16);

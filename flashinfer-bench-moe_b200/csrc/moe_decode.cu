@@ -38,9 +38,11 @@
 // MMA'd into its own TMEM buffer and promoted by s1 * a_scale into fp32
 // registers (the per-128-K block scales are applied exactly).  Four sets of four
 // epilogue warps take the K-blocks kb = j (mod 4), so four K-blocks are in flight
-// in the epilogue; their partial sums are added in set order.  Split-K: when few
-// units exist the permute kernel sets splits[0] = S > 1; the S items of a unit
-// write fp32 partials and the item that arrives last adds them in split order.
+// in the epilogue; their partial sums are added in set order.  Work is balanced
+// "stream-K" style: the phase's K-blocks, flattened unit-major, are cut into one
+// contiguous range per CTA (see Partition); a unit cut by range boundaries is
+// computed in segments whose fp32 partials the segment that arrives last adds in
+// segment order (deterministic).
 // Warps: w0 producer (TMA + cp.async), w1 MMA issuer, w2-w3 idle, w4-w19 epilogue.
 //
 // GEMM2 phase.  Work unit = (block) x (slice h of 128 hidden columns): A = 128
@@ -48,8 +50,9 @@
 // f16 scale, see w2_block_exponent) by eight converter warps into the UMMA
 // layout; B = the block's f16 intermediate rows
 // (TMA).  TMEM accumulates the whole K = 2048 (no promotion: the scale is in the
-// operand).  Split-K: splits[1] = S > 1 shares a unit's 16 K-blocks among S items
-// that write separate planes of pair rows; the combine adds the planes.
+// operand).  Stream-K as in GEMM1, with ranges of >= 16 K-blocks, so a unit has at
+// most two segments; segment s writes plane s of the pair rows and the combine
+// adds a unit's planes.
 // Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 intermediate producer (TMA),
 // w4-w7 and w12-w15 converters, w8-w11 epilogue, the rest idle; then all threads combine.
 #include "fbmoe_common.cuh"
@@ -88,11 +91,13 @@ constexpr int kP1Xch = kP1WScale + 2 * kHBlocks * 4;
 constexpr int kP1Tok = kP1Xch + kSets * 128 * kXchStride * 4;
 constexpr int kP1End = kP1Tok + BN * 4;
 // ---- GEMM2 phase layout
-// 8 raw W2 stages (128 KB in flight per SM) and 2 converted stages: the raw ring
-// is what streams from HBM; the converters run at shared-memory speed.
-constexpr int kRawStages = 8;
-constexpr int kConvStages = 2;
-constexpr int kBStages = 6;
+// Raw W2 stages are what streams from HBM (5 x 16 KB in flight per SM).  A
+// converted stage is held until its MMAs complete, and MMA completion latency
+// (~1 us) is long against the conversion (~0.3 us per stage): with 2 converted
+// stages the phase ran at ~23 GB/s per SM, so 4 are kept.
+constexpr int kRawStages = 5;
+constexpr int kConvStages = 4;
+constexpr int kBStages = 4;
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kAhBytes = 2 * 128 * 128;     // f16 W2 tile (two 64-K halves)
 constexpr int kB2Bytes = BN * 256;          // f16 intermediate rows (two 64-K halves)
@@ -129,7 +134,7 @@ struct DecodeArgs {
   const int32_t* row_token;
   const float* row_weight;
   const int32_t* token_rows;
-  const int32_t* splits;
+  int streamk;           // 1: K-block-granular partition with split-K fix-ups; 0: whole units
   int32_t* split_count;
   float* split_part;
   int32_t* blk_ready;
@@ -163,6 +168,64 @@ __device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
   return v;
 }
 
+// Balanced partition of one phase's K-blocks over the CTAs that take part
+// ("stream-K"): the phase's units are flattened unit-major (unit u holds K-blocks
+// [u*len, u*len + len)) and CTA c owns the range [begin(c), begin(c+1)).  A unit
+// cut by range boundaries is computed in segments on different CTAs and fixed up
+// in segment order (deterministic).  With unit_aligned the boundaries fall on
+// unit boundaries, so no unit is cut (used when no split-K buffers exist).
+struct Partition {
+  int total;         // units * len
+  int len;           // K-blocks per unit
+  int g;             // CTAs that take part
+  bool unit_aligned;
+  __device__ int begin(int c) const {
+    if (c >= g) return total;
+    if (unit_aligned) return (int)(((long long)c * (total / len)) / g) * len;
+    return (int)(((long long)c * total) / g);
+  }
+  // the CTA whose range holds K-block x
+  __device__ int owner(int x) const {
+    if (unit_aligned) {
+      const long long nu = total / len;
+      return (int)((((long long)(x / len) + 1) * g + nu - 1) / nu) - 1;
+    }
+    return (int)((((long long)x + 1) * g + total - 1) / total) - 1;
+  }
+  __device__ int first_owner(int u) const { return owner(u * len); }
+  __device__ int nseg(int u) const { return owner(u * len + len - 1) - owner(u * len) + 1; }
+};
+
+// The segment of unit x / len that starts at K-block x and ends before `end`.
+struct Seg {
+  int u, kb0, kb1;
+};
+__device__ __forceinline__ Seg seg_at(const Partition& P, int x, int end) {
+  Seg sg;
+  sg.u = x / P.len;
+  sg.kb0 = x % P.len;
+  sg.kb1 = min(P.len, sg.kb0 + (end - x));
+  return sg;
+}
+
+// Phase partitions.  Stream-K: GEMM1 ranges hold >= 8 K-blocks (a unit has up to 8
+// segments; a CTA writes at most 2 partials: its first and its last unit); GEMM2
+// ranges hold >= 16 K-blocks = one unit, so a unit has at most 2 segments = planes.
+__device__ __forceinline__ Partition gemm1_partition(int nb, bool streamk) {
+  const int units = nb * kG1Slices, total = units * kHBlocks;
+  const int g = streamk ? max(1, min((int)gridDim.x, total / 8)) : max(1, min((int)gridDim.x, units));
+  return Partition{total, kHBlocks, g, !streamk};
+}
+__device__ __forceinline__ Partition gemm2_partition(int nb, bool streamk) {
+  const int units = nb * kG2Slices, total = units * kIBlocks;
+  const int g = streamk ? max(1, min((int)gridDim.x, total / kIBlocks)) : max(1, min((int)gridDim.x, units));
+  return Partition{total, kIBlocks, g, !streamk};
+}
+// fp32 partial slot of CTA c's segment of unit u: 2c for its first unit, 2c + 1 for its last.
+__device__ __forceinline__ int partial_slot(const Partition& P, int c, int u) {
+  return 2 * c + (u == P.begin(c) / P.len ? 0 : 1);
+}
+
 // ============================================================== GEMM1 phase
 __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
                                             int nb, volatile int* sAbort, volatile int* sLast) {
@@ -180,10 +243,8 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
   uint64_t* drain = tempty + kBufs1;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_units = nb * kG1Slices;
-  const int n_split = a.splits[0];               // K splits per unit
-  const int nk = kHBlocks / n_split;             // K-blocks per work item
-  const int n_items = n_units * n_split;
+  const Partition P = gemm1_partition(nb, a.streamk != 0);
+  const int x_beg = P.begin(blockIdx.x), x_end = P.begin(blockIdx.x + 1);
   auto fail = [&](uint32_t bit) {
     *sAbort = 1;
     atomicOr(a.status, bit);
@@ -199,8 +260,10 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
     uint32_t last_parity[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) last_parity[s] = 0xFFFFFFFFu;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-      const int u = it / n_split, sp = it % n_split;
+    for (int x = x_beg; x < x_end && ok;) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u;
       const int4 blk = a.blocks[u / kG1Slices];
       const int g = u % kG1Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
@@ -214,7 +277,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       }
       const int wrow1 = e * kGemm1N + 64 * g;
       const int wrow2 = wrow1 + kInter;
-      for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutProducer);
@@ -273,8 +336,10 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       uint32_t kbg = 0;
       bool ok = true;
       bool any = false;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        for (int l = 0; l < nk; ++l) {
+      for (int x = x_beg; x < x_end && ok;) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        for (int l = 0; l < sg.kb1 - sg.kb0; ++l) {
           const uint32_t buf = kbg % kBufs1;
           if (!mbar_wait(&tempty[buf], ((kbg / kBufs1) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
               !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
@@ -315,8 +380,11 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
     uint32_t kbg = 0;                  // K-blocks this CTA processed before the current item
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-      const int u = it / n_split, sp = it % n_split;
+    for (int x = x_beg; x < x_end && ok;) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u, nk = sg.kb1 - sg.kb0;
+      const int nseg = P.nseg(u);
       const int4 blk = a.blocks[u / kG1Slices];
       const int g = u % kG1Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
@@ -349,7 +417,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
           break;
         }
         tc_fence_after();
-        const int kb = sp * nk + l;
+        const int kb = sg.kb0 + l;
         const float ws = wsc[kb];
         const float* asc = sAScale + kb * BN;
         float p[16];
@@ -373,9 +441,9 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         break;
       }
       bool last = true;
-      if (n_split > 1) {
-        // publish this item's partial, then find out whether it completes the unit
-        float* part = a.split_part + (size_t)it * 128 * BN;
+      if (nseg > 1) {
+        // publish this segment's partial, then find out whether it completes the unit
+        float* part = a.split_part + (size_t)partial_slot(P, blockIdx.x, u) * 128 * BN;
         for (int i = etid; i < 128 * BN; i += kEpi1Threads) {
           const int r = i / BN, t = i % BN;
           float v = 0.0f;
@@ -385,28 +453,29 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         }
         __threadfence();
         named_barrier_sync(1, kEpi1Threads);
-        if (etid == 0) *sLast = (atomicAdd(&a.split_count[u], 1) == n_split - 1) ? 1 : 0;
+        if (etid == 0) *sLast = (atomicAdd(&a.split_count[u], 1) == nseg - 1) ? 1 : 0;
         named_barrier_sync(1, kEpi1Threads);
         last = *sLast != 0;
         if (last) __threadfence();
       }
       if (last) {
         // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).
-        const float* parts = a.split_part + (size_t)u * n_split * 128 * BN;
+        const int c0 = P.first_owner(u);
         for (int i = etid; i < 64 * BN; i += kEpi1Threads) {
           const int r = i % 64, t = i / 64;
           if (t < nrows) {
             float x1 = 0.0f, x2 = 0.0f;
-            if (n_split == 1) {
+            if (nseg == 1) {
 #pragma unroll
               for (int j = 0; j < G; ++j) {
                 x1 += sXch[(size_t)(j * 128 + r) * kXchStride + t];
                 x2 += sXch[(size_t)(j * 128 + 64 + r) * kXchStride + t];
               }
             } else {
-              for (int q = 0; q < n_split; ++q) {
-                x1 += __ldcg(parts + (size_t)q * 128 * BN + r * BN + t);
-                x2 += __ldcg(parts + (size_t)q * 128 * BN + (64 + r) * BN + t);
+              for (int q = 0; q < nseg; ++q) {  // segment order: deterministic
+                const float* pq = a.split_part + (size_t)partial_slot(P, c0 + q, u) * 128 * BN;
+                x1 += __ldcg(pq + r * BN + t);
+                x2 += __ldcg(pq + (64 + r) * BN + t);
               }
             }
             bool sat = false;
@@ -415,7 +484,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
             if (sat) atomicOr(a.status, kStatusSaturated);
           }
         }
-        if (n_split > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
+        if (nseg > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
         __threadfence();  // the slice's rows are visible before the block counter moves
       }
       named_barrier_sync(1, kEpi1Threads);
@@ -443,10 +512,8 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
   uint64_t* drain = tempty + kBufs2;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_units = nb * kG2Slices;
-  const int n_split = a.splits[1];               // K splits per unit
-  const int nk = kIBlocks / n_split;             // K-blocks per work item
-  const int n_items = n_units * n_split;
+  const Partition P = gemm2_partition(nb, a.streamk != 0);
+  const int x_beg = P.begin(blockIdx.x), x_end = P.begin(blockIdx.x + 1);
   auto fail = [&](uint32_t bit) {
     *sAbort = 1;
     atomicOr(a.status, bit);
@@ -465,8 +532,10 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       int ready_blk = -1;  // block whose intermediate rows are known complete
       uint32_t last_parity[SR > SB ? SR : SB];
       for (int s = 0; s < n; ++s) last_parity[s] = 0xFFFFFFFFu;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        const int u = it / n_split, sp = it % n_split;
+      for (int x = x_beg; x < x_end && ok;) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        const int u = sg.u;
         const int b = u / kG2Slices;
         const int4 blk = a.blocks[b];
         const int h = u % kG2Slices;
@@ -486,7 +555,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
           ready_blk = b;
         }
-        for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&emptyb[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutProducer);
@@ -520,7 +589,10 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       uint32_t ug = 0;
       bool ok = true;
       bool any = false;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ug) {
+      for (int x = x_beg; x < x_end && ok; ++ug) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        const int nk = sg.kb1 - sg.kb0;
         const uint32_t buf = ug % kBufs2;
         if (!mbar_wait(&tempty[buf], ((ug / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
@@ -567,15 +639,17 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     const int ctid = (warp < 8 ? warp - 4 : warp - 8) * 32 + lane;  // 0..255
     Ring rr(SR), cr(SC);
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-      const int u = it / n_split, sp = it % n_split;
+    for (int x = x_beg; x < x_end && ok;) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u;
       const int4 blk = a.blocks[u / kG2Slices];
       const int h = u % kG2Slices;
       const float* sc = a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
       const int kexp = w2_block_exponent(sc);
       // the unit's 16 scales, one per lane: no global load on the per-stage path
       const float lane_scale = __ldg(sc + (lane & (kIBlocks - 1)));
-      for (int kb = sp * nk; kb < (sp + 1) * nk; ++kb) {
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
         if (!mbar_wait(&raw_full[rr.slot], rr.phase, sAbort, kWaitBudgetNs) ||
             !mbar_wait(&c_empty[cr.slot], cr.phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
@@ -622,8 +696,11 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     const int hrow = ew * 32 + lane;
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
     uint32_t ug = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++ug) {
-      const int u = it / n_split, sp = it % n_split;
+    for (int x = x_beg; x < x_end; ++ug) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u;
+      const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
       const int4 blk = a.blocks[u / kG2Slices];
       const int h = u % kG2Slices;
       const int r0 = blk.y, nrows = blk.z;
@@ -657,7 +734,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
 // that the permute kernel zeroed): out[t, 8c .. 8c+7] for every token t and
 // column group c, spread over all threads of the grid.  The token's pair rows are
 // summed over planes, then slots, in fixed order (deterministic), in fp32.
-__device__ __forceinline__ void combine_phase(const DecodeArgs& a, volatile int* sAbort) {
+__device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volatile int* sAbort) {
   if (threadIdx.x == 0) {
     __threadfence();  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
     atomicAdd(a.grid_sync, 1);
@@ -673,7 +750,7 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, volatile int*
   }
   __syncthreads();
   if (*sAbort) return;
-  const int planes = a.splits[1];
+  const Partition P2 = gemm2_partition(nb, a.streamk != 0);
   constexpr int kGroupsPerRow = kHidden / 8;
   const int tasks = a.T * kGroupsPerRow;
   // consecutive tasks go to different CTAs, so a small T still uses many SMs
@@ -686,17 +763,22 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, volatile int*
     const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
     const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
     const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
-    for (int s = 0; s < planes; ++s) {
+    // planes of each slot's pair row: the GEMM2 segments of its unit (block = row / 16, slice = col / 128)
+    int np[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+      np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + (int)(col / 128)) : 0;
+    for (int s = 0; s < 2; ++s) {
       // the plane's (up to 8) rows are loaded together: one L2 round trip per plane
       uint4 v[kTopK];
 #pragma unroll
       for (int k = 0; k < kTopK; ++k)
-        v[k] = rows[k] >= 0 ? __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)s * a.plane_elems +
-                                                                    (size_t)rows[k] * kHidden + col))
-                            : make_uint4(0u, 0u, 0u, 0u);
+        v[k] = s < np[k] ? __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)s * a.plane_elems +
+                                                                 (size_t)rows[k] * kHidden + col))
+                         : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
       for (int k = 0; k < kTopK; ++k) {
-        if (rows[k] >= 0) {
+        if (s < np[k]) {
           const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -806,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     tc_fence_after();
     if (!*sAbort) gemm2_phase(a, sm, bars2, tmem_base, nb, sAbort);
     __syncthreads();  // this CTA's pair rows are all written
-    combine_phase(a, sAbort);
+    combine_phase(a, nb, sAbort);
   }
 
   tc_fence_before();
@@ -844,7 +926,7 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.row_token = reinterpret_cast<const int32_t*>(ws + L.row_token);
   a.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
   a.token_rows = reinterpret_cast<const int32_t*>(ws + L.token_rows);
-  a.splits = reinterpret_cast<const int32_t*>(ws + L.splits);
+  a.streamk = L.split_items > 0 ? 1 : 0;
   a.split_count = reinterpret_cast<int32_t*>(ws + L.split_count);
   a.split_part = reinterpret_cast<float*>(ws + L.split_part);
   a.blk_ready = reinterpret_cast<int32_t*>(ws + L.blk_ready);

@@ -12,8 +12,8 @@
 // blocks GEMM1 gathers token rows itself; for 128-row blocks moe_gather.cu
 // copies them.  Padding rows get row_token = -1.
 //
-// It also chooses the K splits of the decode GEMMs for this call from the block
-// count (see pick_split) and clears the split-K arrival counters.
+// It also clears the arrival counters of the decode kernel (stream-K fix-up,
+// per-block readiness, grid arrival).
 //
 // Tokens are processed in chunks of 1024, one CTA of 1024 threads per chunk.
 // With one chunk (T <= 1024) a single CTA counts, scans and scatters.  With more,
@@ -43,29 +43,7 @@ struct PermuteSmem {
   uint16_t wpre[kMaxLocal][kWordsPerChunk];
   int scan_tmp[2][kMaxLocal / 32];
   int n_blocks;
-  int split1;
 };
-
-// Smallest split S of `units` work units (from `cand`, ascending) whose S*units
-// items fill `sms` CTAs to >= 85% of their last wave; otherwise the best one.
-// Splits cost a partial write/read per item, hence the preference for small S.
-__device__ int pick_split(int units, int sms, const int* cand, int ncand, int max_items) {
-  int best = 1;
-  float best_eff = -1.0f;
-  for (int i = 0; i < ncand; ++i) {
-    const int S = cand[i];
-    const long items = (long)units * S;
-    if (S > 1 && items > max_items) break;
-    const float waves = (float)items / (float)sms;
-    const float eff = waves / ceilf(waves);
-    if (eff >= 0.85f) return S;
-    if (eff > best_eff + 0.02f) {
-      best_eff = eff;
-      best = S;
-    }
-  }
-  return best;
-}
 
 // Per-chunk expert counts: CTA c counts tokens [1024c, 1024c + 1024).
 __global__ void __launch_bounds__(kThreads) permute_count_kernel(const int32_t* __restrict__ topk_idx, int T,
@@ -190,23 +168,15 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
       const int nb_all = min(tot_blocks, max_blocks);
       *n_blocks = nb_all;
       if (tot_blocks > max_blocks) atomicOr(status, kStatusBadTile);
-      int s1 = 1, s2 = 1;
-      if (split_items > 0 && nb_all > 0) {
-        const int c1[5] = {1, 2, 4, 7, 8};  // divisors of the 56 K-blocks of GEMM1
-        const int c2[3] = {1, 2, 4};        // divisors of the 16 K-blocks of GEMM2
-        s1 = pick_split(nb_all * (kInter / 64), num_sms, c1, 5, split_items);
-        s2 = pick_split(nb_all * (kHidden / 128), num_sms, c2, pair_planes >= 4 ? 3 : pair_planes >= 2 ? 2 : 1,
-                        1 << 30);
-      }
-      splits[0] = s1;
-      splits[1] = s2;
+      // planes of pair rows for the combine kernel (128-row path: always one)
+      splits[0] = 1;
+      splits[1] = 1;
       S.n_blocks = nb_all;
-      S.split1 = s1;
     }
   }
   __syncthreads();
   if (lead) {
-    if (S.split1 > 1) {
+    if (split_items > 0) {  // the decode kernel's stream-K arrival counters, one per GEMM1 unit
       const int units = S.n_blocks * (kInter / 64);
       for (int i = tid; i < units; i += kThreads) split_count[i] = 0;
     }
