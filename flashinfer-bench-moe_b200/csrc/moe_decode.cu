@@ -47,8 +47,8 @@
 //
 // GEMM2 phase.  Work unit = (block) x (slice h of 128 hidden columns): A = 128
 // W2 rows, dequantised on chip to f16 (one HMUL2 by the power-of-two-shifted
-// f16 scale, see w2_block_exponent) by eight converter warps into the UMMA
-// layout; B = the block's f16 intermediate rows
+// f16 scale, see w2_block_exponent) by eight converter warps straight into
+// tensor memory, where the MMA reads it; B = the block's f16 intermediate rows
 // (TMA).  TMEM accumulates the whole K = 2048 (no promotion: the scale is in the
 // operand).  Stream-K as in GEMM1, with ranges of >= 16 K-blocks, so a unit has at
 // most two segments; segment s writes plane s of the pair rows and the combine
@@ -91,22 +91,21 @@ constexpr int kP1Xch = kP1WScale + 2 * kHBlocks * 4;
 constexpr int kP1Tok = kP1Xch + kSets * 128 * kXchStride * 4;
 constexpr int kP1End = kP1Tok + BN * 4;
 // ---- GEMM2 phase layout
-// Raw W2 stages are what streams from HBM (5 x 16 KB in flight per SM).  A
-// converted stage is held until its MMAs complete, and MMA completion latency
-// (~1 us) is long against the conversion (~0.3 us per stage): with 2 converted
-// stages the phase ran at ~23 GB/s per SM, so 4 are kept.
-constexpr int kRawStages = 5;
+// The W2 tile is converted to f16 straight into tensor memory, where the MMA
+// reads its A operand, so shared memory holds only raw W2 and the intermediate
+// rows: 12 raw stages (192 KB of W2 in flight per SM).  Tensor memory: 16 GEMM2
+// accumulators of 16 columns (columns 0-255) and 4 converted stages of 64
+// columns (a 128-row x 128-K f16 tile, two K values per column; columns 256-511).
+constexpr int kRawStages = 12;
 constexpr int kConvStages = 4;
 constexpr int kBStages = 4;
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
-constexpr int kAhBytes = 2 * 128 * 128;     // f16 W2 tile (two 64-K halves)
 constexpr int kB2Bytes = BN * 256;          // f16 intermediate rows (two 64-K halves)
-// TMEM accumulators of GEMM2 items: 32 x 16 columns, so the MMA runs up to 32
-// items ahead of the epilogue.
-constexpr int kBufs2 = 32;
+constexpr int kBufs2 = 16;
+constexpr int kA2Col = kBufs2 * BN;         // first TMEM column of the converted stages
+constexpr int kA2StageCols = 64;
 constexpr int kP2Raw = 0;
-constexpr int kP2Ah = kP2Raw + kRawStages * kRawBytes;
-constexpr int kP2B = kP2Ah + kConvStages * kAhBytes;
+constexpr int kP2B = kP2Raw + kRawStages * kRawBytes;
 constexpr int kP2End = kP2B + kBStages * kB2Bytes;
 constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
 // ---- barriers and flags (not reused across phases)
@@ -119,7 +118,7 @@ constexpr int kTmemCols = 512;                    // one CTA per SM holds all of
 static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
 static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
 static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
-static_assert(kBufs1 * BN <= kTmemCols && kBufs2 * BN <= kTmemCols, "TMEM allocation");
+static_assert(kBufs1 * BN <= kTmemCols && kA2Col + kConvStages * kA2StageCols <= kTmemCols, "TMEM allocation");
 
 struct DecodeArgs {
   CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
@@ -499,7 +498,6 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
                                             int nb, volatile int* sAbort) {
   constexpr int SR = kRawStages, SC = kConvStages, SB = kBStages;
   uint8_t* sRaw = sm + kP2Raw;
-  uint8_t* sAh = sm + kP2Ah;
   uint8_t* sB = sm + kP2B;
   uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
   uint64_t* raw_empty = bars + SR;             // converters done reading it
@@ -609,13 +607,14 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
             break;
           }
           tc_fence_after();
+          // A: the converted stage in TMEM (K = 16 per MMA = 8 columns); B: the two
+          // 64-K halves of the intermediate rows in shared memory
+          const uint32_t a_col = tmem_base + kA2Col + ring.slot * kA2StageCols;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const uint64_t adesc = umma_desc_sw128(smem_u32(sAh + ring.slot * kAhBytes + half * 128 * 128));
-            const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + bring.slot * kB2Bytes + half * BN * 128));
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              mma_f16(d, adesc + 2 * j, bdesc + 2 * j, idesc, (kb | half | j) ? 1u : 0u);
+          for (int j = 0; j < 8; ++j) {
+            const uint64_t bdesc =
+                umma_desc_sw128(smem_u32(sB + bring.slot * kB2Bytes + (j >> 2) * BN * 128)) + 2 * (j & 3);
+            mma_f16_tmem_a(d, a_col + 8 * j, bdesc, idesc, (kb | j) ? 1u : 0u);
           }
           tc_commit(&c_empty[ring.slot]);
           tc_commit(&b_empty[bring.slot]);
@@ -634,9 +633,13 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     __syncwarp();
   } else if ((warp >= 4 && warp < 8) || (warp >= 12 && warp < 16)) {
     // ------------------------------------------------------------ converters
-    // 8 warps; thread c converts 16-byte chunks c, c + 256, c + 512, c + 768 of the
-    // raw tile (row = chunk / 8, K bytes 16 * (chunk % 8)): one HMUL2 per 2 weights.
-    const int ctid = (warp < 8 ? warp - 4 : warp - 8) * 32 + lane;  // 0..255
+    // 8 warps; warp w converts rows 32 (w % 4) .. +31 (its TMEM lane quarter) of
+    // K half (w >= 12) of each K-block: 64 fp8 -> 32 columns of f16 pairs, one
+    // HMUL2 per pair, written to the stage's TMEM columns with one tcgen05.st.
+    const int q4 = warp & 3;
+    const int khalf = warp >= 12 ? 1 : 0;
+    const int r = q4 * 32 + lane;  // W2 row of the tile = TMEM lane
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(q4 * 32) << 16) + kA2Col + 32 * khalf;
     Ring rr(SR), cr(SC);
     bool ok = true;
     for (int x = x_beg; x < x_end && ok;) {
@@ -656,31 +659,27 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           if (lane == 0) fail(kStatusTimeoutConvert);
           break;
         }
+        tc_fence_after();  // the MMAs that read this TMEM stage have completed
         const __half2 sc2 = __half2half2(__float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, kb), kexp)));
         const uint8_t* raw = sRaw + rr.slot * kRawBytes;
-        uint8_t* ah = sAh + cr.slot * kAhBytes;
+        uint32_t o[32];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int c = ctid + 256 * i;
-          const int r = c >> 3, cc = c & 7;
-          const uint4 q = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, cc));
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-          uint32_t o[8];
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, 4 * khalf + i));
+          const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] & 0xFFFFu), __NV_E4M3);
             const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] >> 16), __NV_E4M3);
             const __half2 pl = __hmul2(*reinterpret_cast<const __half2*>(&lo), sc2);
             const __half2 ph = __hmul2(*reinterpret_cast<const __half2*>(&hi), sc2);
-            o[2 * j] = *reinterpret_cast<const uint32_t*>(&pl);
-            o[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&ph);
+            o[8 * i + 2 * j] = *reinterpret_cast<const uint32_t*>(&pl);
+            o[8 * i + 2 * j + 1] = *reinterpret_cast<const uint32_t*>(&ph);
           }
-          uint8_t* dst = ah + (cc >> 2) * (128 * 128);
-          const int c2 = (cc & 3) * 2;
-          *reinterpret_cast<uint4*>(dst + sw128_offset(r, c2)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(dst + sw128_offset(r, c2 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
-        fence_proxy_async_smem();
+        tmem_st32(lane_addr + cr.slot * kA2StageCols, o);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&raw_empty[rr.slot]);
