@@ -43,10 +43,16 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) route_kernel(const float*
   if (blockIdx.x == 0 && threadIdx.x == 0 && status != nullptr) status[0] = 0u;
 
   const int warp = threadIdx.x >> 5;
+  int t = blockIdx.x * kWarpsPerBlock + warp;
+  float x[8];
+  if (t < T) route_dev::load_logits8(logits, t, x);  // issued before the bias load: both in flight together
   float bs[8];
   route_dev::load_bias8(bias, bs);
-  for (int t = blockIdx.x * kWarpsPerBlock + warp; t < T; t += gridDim.x * kWarpsPerBlock)
-    route_dev::route_token(logits, t, bs, scale, topk_idx, topk_w, sh_v[warp], sh_i[warp], sh_s[warp], sh_sel[warp]);
+  for (; t < T; t += gridDim.x * kWarpsPerBlock) {
+    route_dev::route_token(x, t, bs, scale, topk_idx, topk_w, sh_v[warp], sh_i[warp], sh_s[warp], sh_sel[warp]);
+    const int tn = t + gridDim.x * kWarpsPerBlock;
+    if (tn < T) route_dev::load_logits8(logits, tn, x);
+  }
 }
 
 }  // namespace

@@ -153,15 +153,21 @@ __device__ __forceinline__ void load_bias8(const __nv_bfloat16* __restrict__ bia
   }
 }
 
-// The calling warp routes token t: topk_idx/topk_w[t*8 .. t*8+7].  wv, wi, ws:
-// this warp's scratch of 256 entries each; ssel: its scratch of 8.
-__device__ __forceinline__ void route_token(const float* __restrict__ logits, int t, const float (&bs)[8],
-                                            float scale, int32_t* __restrict__ topk_idx,
-                                            float* __restrict__ topk_w, float* wv, int* wi, float* ws, int* ssel) {
+// This lane's 8 logits of token t (experts 8 * lane .. 8 * lane + 7).
+__device__ __forceinline__ void load_logits8(const float* __restrict__ logits, int t, float (&x)[8]) {
   const int lane = threadIdx.x & 31;
   const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExperts + lane * 8);
   const float4 xa = __ldg(lp), xb = __ldg(lp + 1);
-  const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  x[0] = xa.x; x[1] = xa.y; x[2] = xa.z; x[3] = xa.w;
+  x[4] = xb.x; x[5] = xb.y; x[6] = xb.z; x[7] = xb.w;
+}
+
+// The calling warp routes token t from its logits x (load_logits8): topk_idx/topk_w
+// [t*8 .. t*8+7].  wv, wi, ws: this warp's scratch of 256 entries each; ssel: its scratch of 8.
+__device__ __forceinline__ void route_token(const float (&x)[8], int t, const float (&bs)[8], float scale,
+                                            int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* wv,
+                                            int* wi, float* ws, int* ssel) {
+  const int lane = threadIdx.x & 31;
   float s[8], sb[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {

@@ -165,3 +165,24 @@ def test_expert_parallel_shard(oracle_mod, fbmoe_lib, workloads, entry):
     st = oracle_mod.error_stats(out[torch.from_numpy(pick).cuda().long()].cpu(), ref, ATOL, RTOL)
     print(st)
     assert st["frac_pass"] == 1.0, st
+
+
+@pytest.mark.parametrize("T,config", [(40, "standard"), (64, "group")])
+def test_decode_all_256_experts(oracle_mod, fbmoe_lib, workloads, entry, T, config):
+    """Decode path (T <= 64) with all 256 experts local (the N=1 expert-parallel layout): many blocks, so the
+    decode kernel's balanced ranges cut GEMM1 units into several segments and GEMM2 units into two planes."""
+    E = 256
+    w = workloads.make_weights(E, 91, "cuda")
+    inp = workloads.make_inputs(T, seed=17 + T, config=config, device="cuda", E_local=E, weights=w)
+    out = _run(entry, workloads, inp)
+    _check_status(fbmoe_lib, T, E)
+    cpu = _to(inp, "cpu")
+    routing = oracle_mod.route(cpu["routing_logits"], cpu["routing_bias"], 2.5)
+    pick = np.random.default_rng(T).choice(T, size=4, replace=False)
+    ref = oracle_mod.run(*[cpu[k] for k in workloads.ARG_ORDER], tokens=pick, routing=routing)
+    st = oracle_mod.error_stats(out[torch.from_numpy(pick).cuda().long()].cpu(), ref, ATOL, RTOL)
+    print(T, config, st)
+    assert st["nonfinite"] == 0
+    assert st["frac_pass"] == 1.0, st
+    del w
+    torch.cuda.empty_cache()
