@@ -259,6 +259,7 @@ def run_ours(args, world, rank, local):
     }
     if world == 1 and not args.no_sweep:
         line["decode_sweep"] = decode_sweep(peaks)
+        line["quantiser"] = quantiser_point(peaks)
         line["prefill"] = prefill_points(peaks)
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline_ep(inp, E_local, budget_s=args.cpu_budget)
@@ -361,6 +362,19 @@ def decode_sweep(peaks):
     del weights
     return {"config": "config1 decode, 32 local experts, offset 0, L2 flushed between calls",
             "peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"], "points": res}
+
+
+def quantiser_point(peaks, T=8192):
+    """The activation quantiser (bf16 [T,7168] -> e4m3 + [56,T] scales) at T tokens, L2 flushed between calls.
+    HBM roofline: 14,336 B read + 7,168 + 224 B written per token."""
+    import fbmoe_lib as L
+    x = (torch.randn((T, H), device="cuda") * 3).to(torch.bfloat16)
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    ms = time_calls(lambda: L.quantize_act(x), 20, lambda: flush_l2(buf))
+    nbytes = T * (2 * H + H + 4 * (H // 128))
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"T": T, "us_per_call": round(ms * 1e3, 2), "algorithmic_bytes": nbytes, "hbm_gbs": round(gbs, 1),
+            "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)}
 
 
 def prefill_points(peaks):

@@ -68,6 +68,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_error_string.restype = ctypes.c_char_p
         lib.fbmoe_version.argtypes = []
         lib.fbmoe_version.restype = i32
+        lib.fbmoe_quantize_act.argtypes = [vp, i32, vp, vp, vp]
+        lib.fbmoe_quantize_act.restype = i32
         _lib = lib
         return lib
 
@@ -205,6 +207,20 @@ def profile_end():
 
 
 STAGES = ("route", "permute", "gemm1", "gemm2", "combine")
+
+
+def quantize_act(x: torch.Tensor):
+    """bf16 [T, 7168] activations -> (e4m3 [T, 7168], fp32 scale [56, T]): the 1x128 rule of the reference
+    (scale = amax / 448, 1 for an all-zero block; round-to-nearest-even, saturating), i.e. ``fused_moe``'s
+    ``hidden_states`` and ``hidden_states_scale``."""
+    _require(x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 2 and x.size(1) == H,
+             "x must be a contiguous CUDA bfloat16 tensor [T, 7168]")
+    T = x.size(0)
+    q = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty((H // 128, T), dtype=torch.float32, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    _check(load_library().fbmoe_quantize_act(x.data_ptr(), int(T), q.data_ptr(), scale.data_ptr(), stream))
+    return q, scale
 
 
 def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, routed_scaling_factor: float):

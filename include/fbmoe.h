@@ -107,6 +107,14 @@ FBMOE_API int fbmoe_forward_noalloc(const float* routing_logits, const void* rou
 FBMOE_API int fbmoe_route(const float* routing_logits, const void* routing_bias, int T, float routed_scaling_factor,
                 int32_t* topk_idx, float* topk_weights, void* stream);
 
+/* Activation quantiser (the producer of fused_moe's hidden_states and
+ * hidden_states_scale): x bf16 [T, 7168] -> q e4m3 [T, 7168] and scale fp32
+ * [56, T] (transposed, as the operator takes it).  Per row and 128-column block:
+ * scale = amax / 448 (1 for an all-zero block), q = e4m3(clamp(x / scale, +-448)),
+ * round-to-nearest-even -- the reference's 1x128 rule, solution/triton/main.py:
+ * 1476-1488 (there applied to its SwiGLU output).  x 8-byte aligned, q 4-byte. */
+FBMOE_API int fbmoe_quantize_act(const void* x_bf16, int T, void* q_e4m3, float* scale, void* stream);
+
 /* Byte offsets of the forward's intermediate buffers inside the workspace, for
  * inspection by tests.  `offsets` receives FBMOE_LAYOUT_FIELDS values in this
  * order: status, topk_idx, topk_w, token_rows, expert_cnt, expert_poff,

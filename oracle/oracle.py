@@ -115,6 +115,18 @@ def _to_numpy_f32(t):
     return np.asarray(t, dtype=np.float32)
 
 
+def quantize_act_1x128(x: torch.Tensor):
+    """Activation quantiser restated on the CPU: per row and 128-column block, scale = amax / 448 (1 for an
+    all-zero block), q = e4m3(clamp(x / scale, -448, 448)) in fp32 with round-to-nearest-even -- the
+    reference's 1x128 rule, solution/triton/main.py:1476-1488.  x: [T, 7168] (any float dtype, evaluated in
+    fp32).  Returns (q e4m3 [T, 7168], scale fp32 [56, T])."""
+    xf = x.float().reshape(x.size(0), -1, 128)
+    amax = xf.abs().amax(dim=2)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (xf / scale.unsqueeze(2)).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.reshape(x.size(0), -1), scale.t().contiguous()
+
+
 def dequant_act(hidden_states: torch.Tensor, hidden_states_scale: torch.Tensor, rows=None) -> torch.Tensor:
     """A = fp8 * scale with the transposed [H/128, T] scale layout (main.py:2496-2505)."""
     hs = hidden_states.cpu()

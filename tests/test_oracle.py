@@ -96,3 +96,17 @@ def test_oracle_matches_reference_run(oracle_mod, workloads, weights_cache, name
     assert st["max_abs"] <= 2e-2, st
     nz = ref.float().abs().sum(1) > 0
     assert torch.equal(out.float().abs().sum(1) > 0, nz)
+
+
+def test_act_quantiser_restatement_matches_the_input_generator(oracle_mod, workloads):
+    """The oracle's 1x128 activation quantiser (reference main.py:1476-1488) and the synthetic-input generator
+    apply the same rule: identical bytes and scales (fp32 input, zero block, large block)."""
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn((6, 7168), generator=g) * 5
+    x[0, :128] = 0
+    x[1, 128:256] *= 1e6
+    q1, s1 = oracle_mod.quantize_act_1x128(x)
+    q2, s2 = workloads.quantize_act_1x128(x)
+    assert torch.equal(s1, s2)
+    assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8))
+    assert torch.all(s1[0, 0] == 1.0)
