@@ -256,14 +256,19 @@ __device__ __forceinline__ void route_token(const float (&x)[8], int t, const fl
         bi = lane * 8 + i;
       }
     }
-#pragma unroll
-    for (int d = 16; d >= 1; d >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
+    // Warp arg-max with the same order (largest value; among equal values the
+    // smallest index): one redux.max over an order-preserving key of the value,
+    // then the lowest lane holding the maximum (a lane's experts are 8 * lane + i,
+    // and its local scan kept the smallest i).  -0 is folded into +0, as in the
+    // float comparison.
+    {
+      uint32_t ub = __float_as_uint(bv);
+      if (ub == 0x80000000u) ub = 0u;
+      const uint32_t key = (ub & 0x80000000u) ? ~ub : (ub | 0x80000000u);
+      const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+      const int win = __ffs(__ballot_sync(0xffffffffu, key == kmax)) - 1;
+      bv = __shfl_sync(0xffffffffu, bv, win);
+      bi = __shfl_sync(0xffffffffu, bi, win);
     }
     if (r < kTopK) {
       sel[r] = bi;
