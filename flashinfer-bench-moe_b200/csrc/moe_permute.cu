@@ -228,6 +228,113 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
   }
 }
 
+// Decode-sized calls (T <= 64): the same outputs with 3 CTA barriers instead
+// of ~10.  Thread p handles (token p / 8, slot p % 8); a token's rank inside an
+// expert is the number of set bits below it in the expert's 64-bit token mask
+// (token-ascending, order-independent); threads 0..255 also own one expert each
+// for the padded offsets and the block list.
+constexpr int kSmallT = 64;
+constexpr int kSmallThreads = kSmallT * kTopK;  // 512
+
+__global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
+    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, int T, int E_local, int local_offset,
+    int bn, int32_t* __restrict__ expert_cnt, int32_t* __restrict__ expert_poff, int32_t* __restrict__ n_blocks,
+    int4* __restrict__ blocks, int max_blocks, int32_t* __restrict__ row_token, float* __restrict__ row_weight,
+    int32_t* __restrict__ token_rows, uint32_t* __restrict__ status, int32_t* __restrict__ splits,
+    int32_t* __restrict__ split_count, int split_items, int32_t* __restrict__ blk_ready,
+    int32_t* __restrict__ grid_sync) {
+  __shared__ int cnt[kMaxLocal];
+  __shared__ unsigned long long mask[kMaxLocal];
+  __shared__ int poff[kMaxLocal];
+  __shared__ int wsum[2][kMaxLocal / 32];
+  __shared__ int nblk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  pdl_trigger();
+  if (tid < kMaxLocal) {
+    cnt[tid] = 0;
+    mask[tid] = 0ull;
+  }
+  __syncthreads();
+  const int t = tid / kTopK;
+  int e = -1;
+  if (t < T) {
+    e = topk_idx[tid] - local_offset;
+    if ((unsigned)e < (unsigned)E_local) {
+      atomicAdd(&cnt[e], 1);
+      atomicOr(&mask[e], 1ull << t);
+    } else {
+      e = -1;
+    }
+  }
+  __syncthreads();
+  // padded offsets and block counts: warp-inclusive scans, then the earlier warps' totals
+  int c = 0, padded = 0, nb = 0, xo = 0, xb = 0;
+  if (tid < kMaxLocal) {
+    c = tid < E_local ? cnt[tid] : 0;
+    padded = (c + kRowAlign - 1) / kRowAlign * kRowAlign;
+    nb = (c + bn - 1) / bn;
+    xo = padded;
+    xb = nb;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int yo = __shfl_up_sync(0xffffffffu, xo, d), yb = __shfl_up_sync(0xffffffffu, xb, d);
+      if (lane >= d) {
+        xo += yo;
+        xb += yb;
+      }
+    }
+    if (lane == 31) {
+      wsum[0][warp] = xo;
+      wsum[1][warp] = xb;
+    }
+  }
+  __syncthreads();
+  if (tid < kMaxLocal) {
+    int base_o = 0, base_b = 0, tot_o = 0, tot_b = 0;
+#pragma unroll
+    for (int w = 0; w < kMaxLocal / 32; ++w) {
+      base_o += w < warp ? wsum[0][w] : 0;
+      base_b += w < warp ? wsum[1][w] : 0;
+      tot_o += wsum[0][w];
+      tot_b += wsum[1][w];
+    }
+    const int off = base_o + xo - padded, boff = base_b + xb - nb;
+    poff[tid] = off;
+    if (tid < E_local) {
+      expert_cnt[tid] = c;
+      expert_poff[tid] = off;
+      for (int j = 0; j < nb; ++j)
+        if (boff + j < max_blocks) blocks[boff + j] = make_int4(tid, off + j * bn, min(bn, c - j * bn), 0);
+      for (int r = off + c; r < off + padded; ++r) row_token[r] = -1;  // padding rows
+    }
+    if (tid == 0) {
+      expert_poff[E_local] = tot_o;
+      const int nb_all = min(tot_b, max_blocks);
+      *n_blocks = nb_all;
+      nblk = nb_all;
+      if (tot_b > max_blocks) atomicOr(status, kStatusBadTile);
+      splits[0] = 1;  // planes of pair rows for the 128-row combine kernel
+      splits[1] = 1;
+      *grid_sync = 0;
+    }
+  }
+  __syncthreads();
+  // the decode kernel's arrival counters (stream-K fix-up, per-block readiness)
+  if (split_items > 0)
+    for (int i = tid; i < nblk * (kInter / 64); i += kSmallThreads) split_count[i] = 0;
+  for (int i = tid; i < nblk; i += kSmallThreads) blk_ready[i] = 0;
+  if (t < T) {
+    int row = -1;
+    if (e >= 0) {
+      row = poff[e] + __popcll(mask[e] & ((1ull << t) - 1ull));
+      row_token[row] = t;
+      row_weight[row] = topk_w[tid];
+    }
+    token_rows[tid] = row;
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
@@ -241,6 +348,14 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
     if (err != cudaSuccess) return err;
     attr_set[dev] = true;
   }
+  if (T > 0 && T <= kSmallT)
+    return launch_pdl(permute_small_kernel, dim3(1), dim3(kSmallThreads), 0, stream, topk_idx, topk_w, T, E_local,
+        local_offset, bn, reinterpret_cast<int32_t*>(ws + L.expert_cnt), reinterpret_cast<int32_t*>(ws + L.expert_poff),
+        reinterpret_cast<int32_t*>(ws + L.n_blocks), reinterpret_cast<int4*>(ws + L.blocks), L.max_blocks,
+        reinterpret_cast<int32_t*>(ws + L.row_token), reinterpret_cast<float*>(ws + L.row_weight),
+        reinterpret_cast<int32_t*>(ws + L.token_rows), reinterpret_cast<uint32_t*>(ws + L.status),
+        reinterpret_cast<int32_t*>(ws + L.splits), reinterpret_cast<int32_t*>(ws + L.split_count), L.split_items,
+        reinterpret_cast<int32_t*>(ws + L.blk_ready), reinterpret_cast<int32_t*>(ws + L.grid_sync));
   const int n_chunks = (T + kThreads - 1) / kThreads;
   int32_t* chunk_cnt = reinterpret_cast<int32_t*>(ws + L.chunk_cnt);
   if (n_chunks > 1) {

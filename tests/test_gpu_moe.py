@@ -115,7 +115,7 @@ def test_forward_is_deterministic(workloads, entry, gpu_weights32):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("T", [901, 3000])  # one 1024-token chunk; three chunks (multi-CTA permute)
+@pytest.mark.parametrize("T", [48, 901, 3000])  # decode-sized kernel; one 1024-token chunk; three chunks
 def test_permutation_invariants(oracle_mod, fbmoe_lib, workloads, entry, gpu_weights32, T):
     E = 32
     inp = workloads.make_inputs(T, seed=9, config="standard", device="cuda", weights=gpu_weights32)
