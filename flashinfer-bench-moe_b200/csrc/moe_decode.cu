@@ -734,6 +734,26 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
 // column group c, spread over all threads of the grid.  The token's pair rows are
 // summed over planes, then slots, in fixed order (deterministic), in fp32.
 __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volatile int* sAbort) {
+  const Partition P2 = gemm2_partition(nb, a.streamk != 0);
+  constexpr int kGroupsPerRow = kHidden / 8;
+  const int tasks = a.T * kGroupsPerRow;
+  // consecutive tasks go to different CTAs, so a small T still uses many SMs
+  const int first = threadIdx.x * gridDim.x + blockIdx.x;
+  // A task's slot rows and plane counts depend only on the permutation, so the
+  // first task's are fetched before the grid arrival completes.
+  int rows[kTopK], np[kTopK];
+  auto prep = [&](int task) {
+    const int t = task / kGroupsPerRow, h = (task % kGroupsPerRow) * 8 / 128;
+    const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
+    const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
+    rows[0] = ra.x; rows[1] = ra.y; rows[2] = ra.z; rows[3] = ra.w;
+    rows[4] = rb.x; rows[5] = rb.y; rows[6] = rb.z; rows[7] = rb.w;
+    // planes of each slot's pair row: the GEMM2 segments of its unit (block = row / 16, slice h)
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + h) : 0;
+  };
+  if (first < tasks) prep(first);
+
   if (threadIdx.x == 0) {
     __threadfence();  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
     atomicAdd(a.grid_sync, 1);
@@ -749,35 +769,24 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volat
   }
   __syncthreads();
   if (*sAbort) return;
-  const Partition P2 = gemm2_partition(nb, a.streamk != 0);
-  constexpr int kGroupsPerRow = kHidden / 8;
-  const int tasks = a.T * kGroupsPerRow;
-  // consecutive tasks go to different CTAs, so a small T still uses many SMs
-  for (int task = threadIdx.x * gridDim.x + blockIdx.x; task < tasks; task += gridDim.x * kThreads) {
+  for (int task = first; task < tasks; task += gridDim.x * kThreads) {
+    if (task != first) prep(task);
     const int t = task / kGroupsPerRow;
     const size_t col = (size_t)(task % kGroupsPerRow) * 8;
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
-    const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
-    const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
-    // planes of each slot's pair row: the GEMM2 segments of its unit (block = row / 16, slice = col / 128)
-    int np[kTopK];
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k)
-      np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + (int)(col / 128)) : 0;
-    for (int s = 0; s < 2; ++s) {
+    for (int pl = 0; pl < 2; ++pl) {  // planes, then slots: fixed order
       // the plane's (up to 8) rows are loaded together: one L2 round trip per plane
       uint4 v[kTopK];
 #pragma unroll
       for (int k = 0; k < kTopK; ++k)
-        v[k] = s < np[k] ? __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)s * a.plane_elems +
-                                                                 (size_t)rows[k] * kHidden + col))
-                         : make_uint4(0u, 0u, 0u, 0u);
+        v[k] = pl < np[k] ? __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)pl * a.plane_elems +
+                                                                  (size_t)rows[k] * kHidden + col))
+                          : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
       for (int k = 0; k < kTopK; ++k) {
-        if (s < np[k]) {
+        if (pl < np[k]) {
           const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
