@@ -47,14 +47,18 @@
 //
 // GEMM2 phase.  Work unit = (block) x (slice h of 128 hidden columns): A = 128
 // W2 rows, dequantised on chip to f16 (one HMUL2 by the power-of-two-shifted
-// f16 scale, see w2_block_exponent) by eight converter warps straight into
+// f16 scale, see w2_block_exponent) by the converter warps straight into
 // tensor memory, where the MMA reads it; B = the block's f16 intermediate rows
 // (TMA).  TMEM accumulates the whole K = 2048 (no promotion: the scale is in the
 // operand).  Stream-K as in GEMM1, with ranges of >= 16 K-blocks, so a unit has at
 // most two segments; segment s writes plane s of the pair rows and the combine
 // adds a unit's planes.
+// Converting a K-block (shared-memory loads, cvt + HMUL2, tcgen05.st, wait) takes
+// longer than streaming it, so three groups of four converter warps take the
+// K-blocks j = 0, 1, 2 (mod 3): three K-blocks are converted at once.
 // Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 intermediate producer (TMA),
-// w4-w7 and w12-w15 converters, w8-w11 epilogue, the rest idle; then all threads combine.
+// w4-w7, w12-w15 and w16-w19 converter groups, w8-w11 epilogue, w3 idle; then all
+// threads combine.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -98,6 +102,7 @@ constexpr int kP1End = kP1Tok + BN * 4;
 // columns (a 128-row x 128-K f16 tile, two K values per column; columns 256-511).
 constexpr int kRawStages = 12;
 constexpr int kConvStages = 4;
+constexpr int kConvGroups = 3;              // converter groups of 4 warps: {4-7}, {12-15}, {16-19}
 constexpr int kBStages = 4;
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kB2Bytes = BN * 256;          // f16 intermediate rows (two 64-K halves)
@@ -117,6 +122,10 @@ constexpr int kSmemBytes = kOffMisc + 32 + 1024;  // + alignment slack
 constexpr int kTmemCols = 512;                    // one CTA per SM holds all of TMEM
 static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
 static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
+// Every raw stage is converted by one group, and a group's previous c_empty wait
+// already covered the MMA of K-block j - kConvGroups - kConvStages >= j - 2 * kConvStages,
+// so no parity wait below can see a phase two completions old.
+static_assert(kRawStages % kConvGroups == 0 && kConvGroups <= kConvStages, "converter group schedule");
 static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
 static_assert(kBufs1 * BN <= kTmemCols && kA2Col + kConvStages * kA2StageCols <= kTmemCols, "TMEM allocation");
 
@@ -631,20 +640,27 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       }
     }
     __syncwarp();
-  } else if ((warp >= 4 && warp < 8) || (warp >= 12 && warp < 16)) {
+  } else if ((warp >= 4 && warp < 8) || warp >= 12) {
     // ------------------------------------------------------------ converters
-    // 8 warps; warp w converts rows 32 (w % 4) .. +31 (its TMEM lane quarter) of
-    // K half (w >= 12) of each K-block: 64 fp8 -> 32 columns of f16 pairs, one
-    // HMUL2 per pair, written to the stage's TMEM columns with one tcgen05.st.
+    // Group grp (warps 4-7, 12-15, 16-19) converts the CTA's K-blocks j with
+    // j % kConvGroups == grp.  Warp w converts rows 32 (w % 4) .. +31 (its TMEM
+    // lane quarter) of the K-block: 128 fp8 -> 64 columns of f16 pairs, one HMUL2
+    // per pair, written to the stage's TMEM columns with two tcgen05.st.
     const int q4 = warp & 3;
-    const int khalf = warp >= 12 ? 1 : 0;
+    const int grp = warp < 8 ? 0 : (warp - 8) >> 2;
     const int r = q4 * 32 + lane;  // W2 row of the tile = TMEM lane
-    const uint32_t lane_addr = tmem_base + ((uint32_t)(q4 * 32) << 16) + kA2Col + 32 * khalf;
-    Ring rr(SR), cr(SC);
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(q4 * 32) << 16) + kA2Col;
+    int j = 0;  // the CTA's running K-block index in this phase
     bool ok = true;
     for (int x = x_beg; x < x_end && ok;) {
       const Seg sg = seg_at(P, x, x_end);
       x += sg.kb1 - sg.kb0;
+      const int nk = sg.kb1 - sg.kb0;
+      const int first = (grp - j % kConvGroups + kConvGroups) % kConvGroups;  // this group's first K-block
+      if (first >= nk) {
+        j += nk;
+        continue;
+      }
       const int u = sg.u;
       const int4 blk = a.blocks[u / kG2Slices];
       const int h = u % kG2Slices;
@@ -652,42 +668,46 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       const int kexp = w2_block_exponent(sc);
       // the unit's 16 scales, one per lane: no global load on the per-stage path
       const float lane_scale = __ldg(sc + (lane & (kIBlocks - 1)));
-      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
-        if (!mbar_wait(&raw_full[rr.slot], rr.phase, sAbort, kWaitBudgetNs) ||
-            !mbar_wait(&c_empty[cr.slot], cr.phase ^ 1u, sAbort, kWaitBudgetNs)) {
+      for (int l = first; l < nk; l += kConvGroups) {
+        const int jj = j + l, kb = sg.kb0 + l;
+        const int rs = jj % SR, cs = jj % SC;
+        if (!mbar_wait(&raw_full[rs], (uint32_t)(jj / SR) & 1u, sAbort, kWaitBudgetNs) ||
+            !mbar_wait(&c_empty[cs], ((uint32_t)(jj / SC) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutConvert);
           break;
         }
         tc_fence_after();  // the MMAs that read this TMEM stage have completed
         const __half2 sc2 = __half2half2(__float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, kb), kexp)));
-        const uint8_t* raw = sRaw + rr.slot * kRawBytes;
-        uint32_t o[32];
+        const uint8_t* raw = sRaw + rs * kRawBytes;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t o[32];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 qv = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, 4 * khalf + i));
-          const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+          for (int i = 0; i < 4; ++i) {
+            const uint4 qv = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, 4 * half + i));
+            const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] & 0xFFFFu), __NV_E4M3);
-            const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] >> 16), __NV_E4M3);
-            const __half2 pl = __hmul2(*reinterpret_cast<const __half2*>(&lo), sc2);
-            const __half2 ph = __hmul2(*reinterpret_cast<const __half2*>(&hi), sc2);
-            o[8 * i + 2 * j] = *reinterpret_cast<const uint32_t*>(&pl);
-            o[8 * i + 2 * j + 1] = *reinterpret_cast<const uint32_t*>(&ph);
+            for (int k = 0; k < 4; ++k) {
+              const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[k] & 0xFFFFu), __NV_E4M3);
+              const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[k] >> 16), __NV_E4M3);
+              const __half2 pl = __hmul2(*reinterpret_cast<const __half2*>(&lo), sc2);
+              const __half2 ph = __hmul2(*reinterpret_cast<const __half2*>(&hi), sc2);
+              o[8 * i + 2 * k] = *reinterpret_cast<const uint32_t*>(&pl);
+              o[8 * i + 2 * k + 1] = *reinterpret_cast<const uint32_t*>(&ph);
+            }
           }
+          tmem_st32(lane_addr + cs * kA2StageCols + 32 * half, o);
         }
-        tmem_st32(lane_addr + cr.slot * kA2StageCols, o);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&raw_empty[rr.slot]);
-          mbar_arrive(&a_full[cr.slot]);
+          mbar_arrive(&raw_empty[rs]);
+          mbar_arrive(&a_full[cs]);
         }
-        rr.next();
-        cr.next();
       }
+      j += nk;
     }
   } else if (warp >= 8 && warp < 12) {
     // ------------------------------------------------------------ epilogue
@@ -840,11 +860,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     uint64_t* b2 = bars2;
     for (int s = 0; s < kRawStages; ++s) {
       mbar_init(&b2[s], 1);
-      mbar_init(&b2[kRawStages + s], 8);  // one arrive per converter warp
+      mbar_init(&b2[kRawStages + s], 4);  // one arrive per warp of the converting group
     }
     b2 += 2 * kRawStages;
     for (int s = 0; s < kConvStages; ++s) {
-      mbar_init(&b2[s], 8);
+      mbar_init(&b2[s], 4);
       mbar_init(&b2[kConvStages + s], 1);
     }
     b2 += 2 * kConvStages;
