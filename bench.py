@@ -165,7 +165,9 @@ def ep_inputs(world, rank):
     return inp, E_local, off
 
 
-def make_step(inp, world, rank):
+def make_step(inp, world, rank, exchange=None):
+    """One timed step: the operator on this rank's experts plus the cross-rank combine, either the fused
+    peer-memory scatter (``exchange``, a fbmoe_ep.PeerExchange) or fp32 partial + NCCL reduce-scatter."""
     import fbmoe_lib as L
     args = [inp[k] for k in ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale",
                              "gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
@@ -177,6 +179,12 @@ def make_step(inp, world, rank):
         def step():
             L.forward(*args, off, scale, out=out, check=False)
             return out
+        return step, out
+    if exchange is not None:
+        out = torch.empty((T // world, H), dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            return exchange.forward(*args, scale, out=out, check=False)
         return step, out
     import fbmoe_ep
     partial = torch.empty((T, H), dtype=torch.float32, device="cuda")
@@ -201,7 +209,11 @@ def run_ours(args, world, rank, local):
     import fbmoe_lib as L
     peaks = load_peaks()
     inp, E_local, off = ep_inputs(world, rank)
-    step, out = make_step(inp, world, rank)
+    exchange = None
+    if world > 1 and args.combine == "p2p":
+        import fbmoe_ep
+        exchange = fbmoe_ep.PeerExchange(T_EP)
+    step, out = make_step(inp, world, rank, exchange)
     for _ in range(args.warmup):
         step()
     barrier(world)
@@ -244,7 +256,11 @@ def run_ours(args, world, rank, local):
                 "stage_ms_per_step": {k: round(v, 4) for k, v in per_stage.items()}, "local_pairs": pairs,
                 "active_local_experts": active}
 
-    e2e = run_e2e(args, world, rank, inp, E_local, off)
+    e2e = run_e2e(args, world, rank, inp, E_local, off, exchange)
+    if exchange is not None:
+        exchange.close()
+    combine = ("none" if world == 1 else "GEMM2 epilogue stores pair rows into the owner's buffer over NVLink "
+               "(CUDA IPC), owner sums slots" if exchange is not None else "nccl reduce_scatter fp32")
     line = {
         "metric": "tokens/s per MoE layer call (DS-V3 FP8 MoE, T=8192, 256 experts, EP over N GPUs)",
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -252,9 +268,10 @@ def run_ours(args, world, rank, local):
         "scaling": "strong", "vs_baseline": None, "dtype": "fp8_e4m3 GEMM1 / f16 GEMM2, fp32 accumulate",
         "data": "synthetic (seeded N(0,1) activations/logits, N(0,0.02) weights, FP8 block-quantised)",
         "config": {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
-                   "parallelism": f"ep{world}", "combine": "none" if world == 1 else "nccl reduce_scatter fp32",
+                   "parallelism": f"ep{world}", "combine": combine,
                    "l2": "inputs larger than L2 (weights %.1f GB per GPU)" % (E_local * BYTES_PER_EXPERT / 1e9)},
-        "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_forward(T_EP, E_local) * args.steps,
+        "roofline": roofline, "e2e": e2e,
+        "gpu_launches": launches_per_forward(T_EP, E_local, world, exchange is not None) * args.steps,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_sweep:
@@ -266,7 +283,7 @@ def run_ours(args, world, rank, local):
     return line
 
 
-def run_e2e(args, world, rank, inp, E_local, off):
+def run_e2e(args, world, rank, inp, E_local, off, exchange=None):
     """Public API with host buffers: every step copies its activations H2D from pinned memory, runs fused_moe
     (+ the EP combine) and copies this rank's output rows D2H.  Steps are pipelined the way a server would run
     them: two device buffer sets, H2D on one copy stream and D2H on another, so step i+1's upload and step i-1's
@@ -282,7 +299,7 @@ def run_e2e(args, world, rank, inp, E_local, off):
     out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out_host[0].numel() * out_host[0].element_size()
-    if world > 1:
+    if world > 1 and exchange is None:
         import fbmoe_ep
         partial = torch.empty((T_EP, H), dtype=torch.float32, device="cuda")
         shard = torch.empty((rows, H), dtype=torch.float32, device="cuda")
@@ -308,6 +325,9 @@ def run_e2e(args, world, rank, inp, E_local, off):
         if world == 1:
             L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w, off,
                       inp["routed_scaling_factor"], out=out_dev[b])
+        elif exchange is not None:
+            exchange.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w,
+                             inp["routed_scaling_factor"], out=out_dev[b])
         else:
             L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w, off,
                       inp["routed_scaling_factor"], out=partial, partial_f32=True)
@@ -337,10 +357,14 @@ def run_e2e(args, world, rank, inp, E_local, off):
             "pipelining": "2 buffer sets; H2D and D2H on their own streams overlap the neighbouring steps' compute"}
 
 
-def launches_per_forward(T, E_local):
+def launches_per_forward(T, E_local, world=1, p2p=False):
     """Our kernels per forward (mirrors forward_core in csrc/moe_capi.cu): T <= 64: router, permute, decode
-    kernel; otherwise router, [per-chunk count], permute, gather, GEMM1, GEMM2, combine."""
+    kernel; otherwise router, [per-chunk count], permute, gather, GEMM1, GEMM2, combine.  The peer-memory
+    expert-parallel path (csrc/moe_ep.cu) always takes the second chain and replaces the combine with a
+    flag-release kernel and the owner's combine."""
     import fbmoe_lib as L
+    if p2p and world > 1:
+        return 7 + (1 if T > 1024 else 0)
     if L.block_rows(T, E_local) == 16:
         return 3
     return 6 + (1 if T > 1024 else 0)
@@ -544,6 +568,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("fbmoe", "reference"), default="fbmoe")
+    ap.add_argument("--combine", choices=("p2p", "nccl"), default="p2p",
+                    help="N>1: GEMM2 stores pair rows into the owners' buffers over NVLink (p2p), or fp32 partial + "
+                         "NCCL reduce-scatter (nccl)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for cpu_baseline")

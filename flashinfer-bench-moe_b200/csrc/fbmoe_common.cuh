@@ -39,6 +39,8 @@ enum StatusBits : uint32_t {
   kStatusBadTile = 1u << 4,
   kStatusTimeoutDrain = 1u << 5,
   kStatusSaturated = 1u << 6,  // an f16 intermediate/pair value was clamped to +-65504
+  kStatusTimeoutPeer = 1u << 7,  // expert parallelism: a peer's pair rows did not arrive in time
+  kStatusBadSlot = 1u << 8,      // expert parallelism: a pair row's (token, slot) was not found
 };
 
 constexpr float kF16Max = 65504.0f;

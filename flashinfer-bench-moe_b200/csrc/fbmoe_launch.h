@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -56,7 +57,19 @@ struct Layout {
 };
 
 // allow_split: reserve the split-K buffers used for 16-row (decode) blocks.
-Layout make_layout(int T, int E_local, bool allow_split = true);
+// force_rows: 128 selects the row-major (prefill) chain for every T.
+Layout make_layout(int T, int E_local, bool allow_split = true, int force_rows = 0);
+
+// Expert parallelism with the combine fused into GEMM2: pair row (token t, slot k)
+// is stored straight into the receive buffer of the rank that owns token t
+// (rows_per_rank consecutive tokens per rank), at pair[o][(t - o * rows_per_rank) * 8 + k].
+// base[o] is rank o's pair region (a CUDA-IPC mapping for o != this rank).
+constexpr int kMaxPeers = 8;
+struct PeerScatter {
+  __half* base[kMaxPeers];
+  int rows_per_rank;
+  int world;  // 0: no scatter, pair rows go to the local workspace
+};
 
 // Decode stream-K: capacity of fp32 partial slots (two per CTA of the decode kernel).
 constexpr int kSplitItems = 1024;
@@ -93,7 +106,8 @@ cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_ap
 // GEMM2 for blocks of 128 rows with the tokens as the MMA M operand; tm_w2raw
 // maps W2 as unswizzled 64-byte x 256-row boxes.
 cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
-                              const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream);
+                              const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream,
+                              const PeerScatter* scatter = nullptr);
 
 // out[t, :] = sum of the token's pair rows, fp32 accumulation; bf16 result, or
 // fp32 (f32_out) for partial sums that another stage combines across ranks.
@@ -105,6 +119,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
-                 size_t workspace_bytes, void* stream, bool allow_split = true);
+                 size_t workspace_bytes, void* stream, bool allow_split = true,
+                 const PeerScatter* scatter = nullptr);
 
 }  // namespace fbmoe

@@ -33,7 +33,7 @@ int choose_block_rows(int T, int E_local) {
   return T <= 64 ? 16 : 128;
 }
 
-Layout make_layout(int T, int E_local, bool allow_split) {
+Layout make_layout(int T, int E_local, bool allow_split, int force_rows) {
   Layout L;
   const size_t tt = (size_t)(T > 0 ? T : 0);
   const int el = E_local > 0 ? E_local : 0;
@@ -59,7 +59,7 @@ Layout make_layout(int T, int E_local, bool allow_split) {
   L.row_token = take((size_t)pcap * 4);
   L.row_weight = take((size_t)pcap * 4);
   L.inter = take((size_t)pcap * kInter * 2);
-  const int bn = choose_block_rows(T, E_local);
+  const int bn = force_rows ? force_rows : choose_block_rows(T, E_local);
   const bool split = allow_split && bn == 16;
   L.pair_planes = split ? kMaxPairPlanes : 1;
   L.split_items = split ? kSplitItems : 0;
@@ -183,20 +183,23 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
-                 size_t workspace_bytes, void* stream_, bool allow_split) {
+                 size_t workspace_bytes, void* stream_, bool allow_split, const PeerScatter* scatter) {
   if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
+  const bool scattering = scatter != nullptr && scatter->world > 0;
   if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale || !gemm1_weights ||
-      !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !out || !workspace)
+      !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || (!out && !scattering) || !workspace)
     return FBMOE_ERR_NULL_POINTER;
   if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
       !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(out, 16) || !aligned(workspace, 256))
     return FBMOE_ERR_MISALIGNED;
-  const Layout L = make_layout(T, E_local, allow_split);
+  // the scatter lives in the row-major GEMM2's epilogue, so it forces that chain
+  const int force_rows = scattering ? 128 : 0;
+  const Layout L = make_layout(T, E_local, allow_split, force_rows);
   if (workspace_bytes < L.total) return FBMOE_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  const int bn = choose_block_rows(T, E_local);
+  const int bn = force_rows ? force_rows : choose_block_rows(T, E_local);
   const int sms = num_sms_of_current_device();
 
   CUtensorMap tm_w1, tm_w2, tm_inter, tm_w2raw, tm_aperm, tm_ascale;
@@ -251,10 +254,12 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
     e = launch_gemm1_rows(&tm_w1, &tm_aperm, &tm_ascale, gemm1_weights_scale, L, ws, sms, stream);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 3, stream);
-    e = launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream);
+    e = launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream,
+                          scattering ? scatter : nullptr);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 4, stream);
-    e = launch_reduce(T, L, ws, out, f32_out, stream);
+    // with the scatter, the owners' combine (moe_ep.cu) replaces the local reduce
+    if (!scattering) e = launch_reduce(T, L, ws, out, f32_out, stream);
   }
   prof_record(fwd, 5, stream);
   return from_cuda(e);

@@ -23,6 +23,12 @@
 // tile's load latency was exposed every step), w3 idle,
 // w4-w11 converters (256 threads, 4 x 16-byte chunks each per step),
 // w12-w15 epilogue (TMEM lane quarter = warp % 4).
+//
+// Expert parallelism (PeerScatter): the epilogue writes pair row (token t, slot k)
+// into the receive buffer of the rank that owns token t, over NVLink for other
+// ranks, instead of the local pair rows; the transfer overlaps the GEMM.  k is
+// the slot whose token_rows entry names this row.  Each epilogue thread ends
+// with a system-scope fence, so a later flag release covers its stores.
 #include <math.h>
 
 #include "fbmoe_common.cuh"
@@ -69,7 +75,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm2_rows_kernel(const __grid_constant__ CUtensorMap tm_w2raw, const __grid_constant__ CUtensorMap tm_inter,
                       const float* __restrict__ w2_scale, const int32_t* __restrict__ n_blocks_ptr,
                       const int4* __restrict__ blocks, const float* __restrict__ row_weight,
-                      __half* __restrict__ pair_out, uint32_t* __restrict__ status) {
+                      __half* __restrict__ pair_out, uint32_t* __restrict__ status,
+                      const int32_t* __restrict__ row_token, const int32_t* __restrict__ token_rows,
+                      const PeerScatter ps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sRaw = sm + kOffRaw;
@@ -296,7 +304,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint4* dst = reinterpret_cast<uint4*>(pair_out + (size_t)(r0 + row) * kHidden + nt * kN);
+      __half* drow = pair_out + (size_t)(r0 + row) * kHidden;
+      bool has_dst = row < nrows;
+      if (ps.world > 0 && has_dst) {
+        const int r = r0 + row;
+        const int t = __ldg(row_token + r);
+        const int4* tr4 = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
+        const int4 ra = __ldg(tr4), rb = __ldg(tr4 + 1);
+        const int k = ra.x == r ? 0 : ra.y == r ? 1 : ra.z == r ? 2 : ra.w == r ? 3
+                    : rb.x == r ? 4 : rb.y == r ? 5 : rb.z == r ? 6 : rb.w == r ? 7 : -1;
+        const int o = t / ps.rows_per_rank;
+        if (k < 0 || o >= ps.world) {
+          atomicOr(status, kStatusBadSlot);
+          has_dst = false;
+        } else {
+          drow = ps.base[o] + ((size_t)(t - o * ps.rows_per_rank) * kTopK + k) * kHidden;
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(drow + nt * kN);
       bool sat = false;
 #pragma unroll 4
       for (int c = 0; c < kN / 16; ++c) {
@@ -310,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const __half a = to_half_sat(p[2 * i] * f, sat), b = to_half_sat(p[2 * i + 1] * f, sat);
           w[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
         }
-        if (row < nrows) {
+        if (has_dst) {
           dst[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
           dst[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
@@ -320,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[buf]);
       if (sat) atomicOr(status, kStatusSaturated);
     }
+    if (ps.world > 0) __threadfence_system();  // peer stores ordered before the signal that follows
   }
 
   tc_fence_before();
@@ -333,7 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
-                              const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream) {
+                              const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream,
+                              const PeerScatter* scatter) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -342,13 +369,16 @@ cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm
     if (err != cudaSuccess) return err;
     attr_set[dev] = true;
   }
+  PeerScatter ps{};
+  if (scatter != nullptr) ps = *scatter;
   const long max_units = (long)L.max_blocks * kNTiles;
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;
   return launch_pdl(gemm2_rows_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, *tm_w2raw, *tm_inter, w2_scale,
                     reinterpret_cast<const int32_t*>(ws + L.n_blocks), reinterpret_cast<const int4*>(ws + L.blocks),
                     reinterpret_cast<const float*>(ws + L.row_weight), reinterpret_cast<__half*>(ws + L.pair_out),
-                    reinterpret_cast<uint32_t*>(ws + L.status));
+                    reinterpret_cast<uint32_t*>(ws + L.status), reinterpret_cast<const int32_t*>(ws + L.row_token),
+                    reinterpret_cast<const int32_t*>(ws + L.token_rows), ps);
 }
 
 }  // namespace fbmoe

@@ -7,14 +7,21 @@ solution/triton/main.py:2558-2564).  Every rank routes all tokens (routing is
 replicated and cheap) and produces the un-rounded fp32 sum over its experts;
 the partials are summed across ranks and rounded to bf16 once.
 
-``combine`` reduce-scatters over token rows: rank r ends with rows
-[r*T/N, (r+1)*T/N) of the layer output.  On NCCL this is one
-``reduce_scatter_tensor``; on backends without it (gloo, used by the CPU tests)
-an all-reduce followed by taking the rank's rows gives the same result.
+Two ways to sum the ranks' contributions; rank r ends with rows
+[r*T/N, (r+1)*T/N) of the layer output either way:
+
+* ``PeerExchange`` (the fast path): GEMM2's epilogue stores every (token, slot)
+  pair row straight into the receive buffer of the token's owner over NVLink
+  peer memory (CUDA IPC), overlapping the GEMM; each owner then sums its tokens'
+  8 slots in slot order.  Same values, same order as the single-GPU operator, so
+  the rows equal its output bit for bit.
+* ``combine`` (the NCCL baseline): each rank's un-rounded fp32 partial over its
+  experts, then one ``reduce_scatter_tensor``; on backends without it (gloo, used
+  by the CPU tests) an all-reduce followed by taking the rank's rows.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -73,3 +80,76 @@ def fused_moe_ep(routing_logits, routing_bias, hidden_states, hidden_states_scal
                                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
                                 routed_scaling_factor, partial_f32=True)
     return combine(partial, group)
+
+
+def owner_of(t: int, T: int, world: int) -> int:
+    """Rank that owns output token t (rows_per_rank consecutive tokens per rank)."""
+    row_range(0, world, T)  # validates T % world
+    return t // (T // world)
+
+
+class PeerExchange:
+    """Receive buffers of every rank for the fused GEMM2 scatter, mapped into this process.
+
+    Collective: every rank of ``group`` constructs it with the same T (token count per
+    call, a multiple of the world size) and E_local = 256 / world.  Buffers are
+    exchanged once (CUDA IPC handles over ``all_gather_object``); each ``forward``
+    is one expert-parallel MoE layer with no NCCL call in the data path."""
+
+    def __init__(self, T: int, group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None):
+        import fbmoe_lib
+        self.lib = fbmoe_lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.T = int(T)
+        self.E_local, self.offset = shard(self.rank, self.world)
+        row_range(self.rank, self.world, self.T)  # validates T % world
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        nbytes = fbmoe_lib.ep_recv_bytes(self.T, self.world)
+        if nbytes == 0:
+            raise ValueError(f"no receive buffer for T={T}, world={self.world}")
+        self.local = fbmoe_lib.ipc_alloc(nbytes)
+        handles: List[Optional[bytes]] = [None] * self.world
+        dist.all_gather_object(handles, fbmoe_lib.ipc_handle(self.local), group=group)
+        self.opened: List[int] = []
+        ptrs = []
+        for o in range(self.world):
+            if o == self.rank:
+                ptrs.append(self.local)
+            else:
+                p = fbmoe_lib.ipc_open(handles[o])
+                self.opened.append(p)
+                ptrs.append(p)
+        self.ptrs: Sequence[int] = ptrs
+        self.workspace = torch.empty(fbmoe_lib.ep_workspace_size(self.T, self.E_local), dtype=torch.uint8,
+                                     device=self.device)
+        self.epoch = 0
+        dist.barrier(group=group)  # every rank's buffer exists and is mapped before the first send
+
+    def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor,
+                out: Optional[torch.Tensor] = None, check: bool = True) -> torch.Tensor:
+        """This rank's token rows [T/world, 7168] bf16 of the layer output (its expert shard's weights)."""
+        self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFF0 else 1
+        if out is None:
+            out = torch.empty((self.T // self.world, H), dtype=torch.bfloat16, device=self.device)
+        inputs = (routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                  gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, self.offset, routed_scaling_factor)
+        self.lib.ep_send(inputs, self.rank, self.world, self.ptrs, self.epoch, self.workspace, check=check)
+        return self.lib.ep_recv(self.local, self.T, self.rank, self.world, self.epoch, out, self.workspace)
+
+    def status(self) -> int:
+        """Device status word of the last forward (synchronises the current stream)."""
+        return self.lib.read_status(self.workspace)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: call on every rank)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no peer still writes into this rank's buffer
+        for p in self.opened:
+            self.lib.ipc_close(p)
+        self.opened = []
+        if self.local:
+            self.lib.ipc_free(self.local)
+            self.local = 0

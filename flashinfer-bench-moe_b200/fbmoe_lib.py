@@ -70,6 +70,29 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_version.restype = i32
         lib.fbmoe_quantize_act.argtypes = [vp, i32, vp, vp, vp]
         lib.fbmoe_quantize_act.restype = i32
+        u32 = ctypes.c_uint32
+        lib.fbmoe_ep_recv_bytes.argtypes = [i32, i32]
+        lib.fbmoe_ep_recv_bytes.restype = sz
+        lib.fbmoe_ep_workspace_size.argtypes = [i32, i32]
+        lib.fbmoe_ep_workspace_size.restype = sz
+        lib.fbmoe_forward_ep_send.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, i32, vp, u32,
+                                              vp, sz, vp]
+        lib.fbmoe_forward_ep_send.restype = i32
+        lib.fbmoe_forward_ep_recv.argtypes = [vp, i32, i32, i32, u32, vp, vp, vp]
+        lib.fbmoe_forward_ep_recv.restype = i32
+        lib.fbmoe_forward_ep.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, i32, vp, u32, vp,
+                                         vp, sz, vp]
+        lib.fbmoe_forward_ep.restype = i32
+        lib.fbmoe_ipc_alloc.argtypes = [sz, ctypes.POINTER(vp)]
+        lib.fbmoe_ipc_alloc.restype = i32
+        lib.fbmoe_ipc_free.argtypes = [vp]
+        lib.fbmoe_ipc_free.restype = i32
+        lib.fbmoe_ipc_handle.argtypes = [vp, vp]
+        lib.fbmoe_ipc_handle.restype = i32
+        lib.fbmoe_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+        lib.fbmoe_ipc_open.restype = i32
+        lib.fbmoe_ipc_close.argtypes = [vp]
+        lib.fbmoe_ipc_close.restype = i32
         _lib = lib
         return lib
 
@@ -248,3 +271,80 @@ def read_status(workspace: torch.Tensor) -> int:
     if rc not in (0, -6):
         _check(rc)
     return int(st.value)
+
+
+# ---------------------------------------------------------------- expert parallelism over peer memory
+IPC_HANDLE_BYTES = 64
+
+
+def ep_recv_bytes(T: int, world: int) -> int:
+    """Bytes of one rank's receive buffer for the fused GEMM2 scatter (0 if T % world != 0)."""
+    return int(load_library().fbmoe_ep_recv_bytes(int(T), int(world)))
+
+
+def ep_workspace_size(T: int, E_local: int) -> int:
+    return int(load_library().fbmoe_ep_workspace_size(int(T), int(E_local)))
+
+
+def ipc_alloc(nbytes: int) -> int:
+    """A zeroed device buffer (cudaMalloc) that other processes can map; returns its address."""
+    ptr = ctypes.c_void_p()
+    _check(load_library().fbmoe_ipc_alloc(int(nbytes), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_free(ptr: int) -> None:
+    _check(load_library().fbmoe_ipc_free(ptr))
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(load_library().fbmoe_ipc_handle(ptr, buf))
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    _require(len(handle) == IPC_HANDLE_BYTES, "bad IPC handle")
+    ptr = ctypes.c_void_p()
+    _check(load_library().fbmoe_ipc_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(load_library().fbmoe_ipc_close(ptr))
+
+
+def _ptr_array(ptrs):
+    arr = (ctypes.c_void_p * len(ptrs))()
+    for i, p in enumerate(ptrs):
+        arr[i] = int(p)
+    return arr
+
+
+def ep_send(inputs, rank: int, world: int, peer_ptrs, epoch: int, workspace: torch.Tensor,
+            check: bool = True) -> None:
+    """Route .. GEMM2 on this rank's experts; GEMM2 stores each pair row into its owner's receive buffer
+    (``peer_ptrs[o]`` = rank o's buffer address in this process), then flags every peer with ``epoch``.
+    ``inputs``: the ten ``fused_moe`` arguments in order."""
+    (logits, bias, hs, hs_scale, w1, s1, w2, s2, offset, scale) = inputs
+    if check:
+        T, E = check_inputs(logits, bias, hs, hs_scale, w1, s1, w2, s2, offset)
+    else:
+        T, E = hs.size(0), w1.size(0)
+    _require(len(peer_ptrs) == world, "one receive buffer per rank is required")
+    stream = torch.cuda.current_stream(hs.device).cuda_stream
+    _check(load_library().fbmoe_forward_ep_send(
+        logits.data_ptr(), bias.data_ptr(), hs.data_ptr(), hs_scale.data_ptr(), w1.data_ptr(), s1.data_ptr(),
+        w2.data_ptr(), s2.data_ptr(), int(T), int(E), int(offset), float(scale), int(rank), int(world),
+        _ptr_array(peer_ptrs), int(epoch), workspace.data_ptr(), int(workspace.numel()), stream))
+
+
+def ep_recv(my_ptr: int, T: int, rank: int, world: int, epoch: int, out: torch.Tensor,
+            workspace: torch.Tensor) -> torch.Tensor:
+    """Wait for every rank's flag of ``epoch`` and write this rank's tokens' output rows (bf16 [T/world, 7168])."""
+    _require(out.is_cuda and out.dtype == torch.bfloat16 and out.is_contiguous()
+             and tuple(out.shape) == (T // world, H), "bad `out` tensor")
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    _check(load_library().fbmoe_forward_ep_recv(my_ptr, int(T), int(rank), int(world), int(epoch), out.data_ptr(),
+                                                workspace.data_ptr(), stream))
+    return out

@@ -127,8 +127,9 @@ FBMOE_API int fbmoe_block_rows(int T, int E_local);
 
 /* Reads the device status word of the last forward on this workspace
  * (synchronises `stream`).  0 = clean; non-zero = a bounded wait expired inside
- * a kernel (bit 0 producer, 1 MMA, 2 epilogue, 3 converter, 5 drain) or the
- * block list overflowed (bit 4). */
+ * a kernel (bit 0 producer, 1 MMA, 2 epilogue, 3 converter, 5 drain, 7 peer
+ * flags of an expert-parallel combine), the block list overflowed (bit 4), an f16
+ * value was clamped (bit 6) or a pair row's slot was not found (bit 8). */
 FBMOE_API int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream);
 
 /* Stage timing for measurement: after fbmoe_profile_begin(n), the next n
@@ -139,6 +140,50 @@ FBMOE_API int fbmoe_read_status(const void* workspace, uint32_t* status, void* s
  * memory); the reference has wall-clock timing only (main.py:2611-2624). */
 FBMOE_API int fbmoe_profile_begin(int max_forwards);
 FBMOE_API int fbmoe_profile_end(float* stage_ms, int* n_forwards);
+
+/* ---- Expert parallelism with the combine fused into GEMM2 (NVLink peer memory).
+ * Replaces the reference's single-GPU combine (reduce_add_kernel, main.py:1604-1714)
+ * and the cross-rank sum of partial outputs for an expert-parallel layer sharded by
+ * local_expert_offset (main.py:2558-2564).  Rank r of `world` (1..8) holds experts
+ * [r*E_local, (r+1)*E_local) with E_local*world == 256 and owns output tokens
+ * [r*T/world, (r+1)*T/world); T % world == 0; every rank passes the same routing
+ * inputs and hidden states (replicated).  peer_recv[o] is rank o's receive buffer
+ * (fbmoe_ep_recv_bytes bytes from fbmoe_ipc_alloc, mapped into this process with
+ * fbmoe_ipc_open; peer_recv[rank] is this rank's own).  epoch: 1, 2, 3, ... per
+ * call, the same on every rank.
+ * _send: route .. GEMM2 on this rank's experts; GEMM2 stores each pair row into
+ *   its owner's buffer; then releases this rank's flag on every peer.
+ * _recv: waits (bounded, status bit 7) for every rank's flag of `epoch`, then
+ *   out_rows_bf16 [T/world, 7168] = the sum of each owned token's 8 pair rows in
+ *   slot order -- equal, bit for bit, to fbmoe_forward with all 256 experts.
+ *   The status word is the one of `workspace` (fbmoe_read_status).
+ * fbmoe_forward_ep = _send then _recv.  Workspace: fbmoe_ep_workspace_size. */
+FBMOE_API size_t fbmoe_ep_recv_bytes(int T, int world);
+FBMOE_API size_t fbmoe_ep_workspace_size(int T, int E_local);
+FBMOE_API int fbmoe_forward_ep_send(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                                    const float* hidden_states_scale, const void* gemm1_weights,
+                                    const float* gemm1_weights_scale, const void* gemm2_weights,
+                                    const float* gemm2_weights_scale, int T, int E_local, int local_expert_offset,
+                                    float routed_scaling_factor, int rank, int world, void* const* peer_recv,
+                                    uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
+FBMOE_API int fbmoe_forward_ep_recv(const void* my_recv, int T, int rank, int world, uint32_t epoch,
+                                    void* out_rows_bf16, void* workspace, void* stream);
+FBMOE_API int fbmoe_forward_ep(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                               const float* hidden_states_scale, const void* gemm1_weights,
+                               const float* gemm1_weights_scale, const void* gemm2_weights,
+                               const float* gemm2_weights_scale, int T, int E_local, int local_expert_offset,
+                               float routed_scaling_factor, int rank, int world, void* const* peer_recv,
+                               uint32_t epoch, void* out_rows_bf16, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* Device buffers shared across processes (cudaMalloc + CUDA IPC).  A handle is
+ * FBMOE_IPC_HANDLE_BYTES opaque bytes; open it in every other process of the node. */
+#define FBMOE_IPC_HANDLE_BYTES 64
+FBMOE_API int fbmoe_ipc_alloc(size_t bytes, void** ptr);
+FBMOE_API int fbmoe_ipc_free(void* ptr);
+FBMOE_API int fbmoe_ipc_handle(const void* ptr, void* handle_out);
+FBMOE_API int fbmoe_ipc_open(const void* handle, void** ptr);
+FBMOE_API int fbmoe_ipc_close(void* ptr);
 
 FBMOE_API const char* fbmoe_error_string(int code);
 

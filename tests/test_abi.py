@@ -83,3 +83,44 @@ def test_quantizers_roundtrip(workloads):
     assert torch.allclose(deqw, w, rtol=0.07, atol=1e-5)
     z, zs = workloads.quantize_act_1x128(torch.zeros(2, 7168))
     assert (zs == 1.0).all() and (z.float() == 0).all()
+
+
+def test_expert_parallel_entry_points_validate_without_launching(fbmoe_lib):
+    lib = fbmoe_lib.load_library()
+    nul = None
+    assert fbmoe_lib.ep_recv_bytes(8192, 8) == 256 + 2 * 1024 * 8 * 7168 * 2
+    assert fbmoe_lib.ep_recv_bytes(100, 3) == 0 and fbmoe_lib.ep_recv_bytes(8, 9) == 0
+    assert fbmoe_lib.ep_workspace_size(8, 32) == lib.fbmoe_ep_workspace_size(8, 32) > 0
+    # the expert-parallel workspace is the row-major chain's at every T (no split-K buffers)
+    assert fbmoe_lib.ep_workspace_size(8192, 32) == fbmoe_lib.workspace_layout(8192, 32)["total"]
+    assert 0 < fbmoe_lib.ep_workspace_size(8, 128)
+
+    def send(T, E, offset, rank, world, peers, epoch=1):
+        return lib.fbmoe_forward_ep_send(nul, nul, nul, nul, nul, nul, nul, nul, T, E, offset, 2.5, rank, world,
+                                         peers, epoch, nul, 0, nul)
+
+    two = fbmoe_lib._ptr_array([16, 32])
+    assert send(64, 128, 0, 0, 3, two) == -1          # 256 experts do not split over 3 ranks
+    assert send(64, 64, 0, 0, 2, two) == -1           # E_local * world != 256
+    assert send(63, 128, 0, 0, 2, two) == -1          # T not a multiple of the world size
+    assert send(64, 128, 0, 1, 2, two) == -1          # offset != rank * E_local
+    assert send(64, 128, 128, 2, 2, two) == -1        # rank outside the world
+    assert send(64, 128, 0, 0, 2, two, epoch=0) == -1  # epoch 0 is reserved
+    assert send(64, 128, 0, 0, 2, None) == -3         # no peer table
+    assert send(64, 128, 0, 0, 2, fbmoe_lib._ptr_array([16, 0])) == -3
+    assert send(64, 128, 0, 0, 2, fbmoe_lib._ptr_array([16, 40])) == -4  # misaligned peer buffer
+    assert send(0, 128, 0, 0, 2, two) == 0            # T == 0 is a no-op
+    assert lib.fbmoe_forward_ep_recv(nul, 64, 0, 2, 0, nul, nul, nul) == -1
+    assert lib.fbmoe_forward_ep_recv(nul, 64, 0, 2, 1, nul, nul, nul) == -3
+    assert lib.fbmoe_forward_ep_recv(nul, 0, 0, 2, 1, nul, nul, nul) == 0
+    assert lib.fbmoe_ipc_alloc(0, None) == -3
+    assert lib.fbmoe_ipc_handle(None, None) == -3 and lib.fbmoe_ipc_open(None, None) == -3
+    assert lib.fbmoe_ipc_free(None) == 0 and lib.fbmoe_ipc_close(None) == 0
+
+
+def test_expert_parallel_token_ownership():
+    import fbmoe_ep
+    assert [fbmoe_ep.owner_of(t, 16, 4) for t in range(16)] == [t // 4 for t in range(16)]
+    assert fbmoe_ep.row_range(3, 4, 16) == (12, 16)
+    with pytest.raises(ValueError):
+        fbmoe_ep.owner_of(0, 10, 4)
