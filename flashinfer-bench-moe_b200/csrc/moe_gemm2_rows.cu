@@ -24,6 +24,11 @@
 // w4-w11 converters (256 threads, 4 x 16-byte chunks each per step),
 // w12-w15 epilogue (TMEM lane quarter = warp % 4).
 //
+// Epilogue stores: each warp converts 64 columns of its 32 rows at a time, stages
+// them in shared memory and writes them with 8 lanes per row, so every store
+// instruction covers four whole 128-byte lines (remote rows cross NVLink in full
+// lines, not in 16-byte pieces).
+//
 // Expert parallelism (PeerScatter): the epilogue writes pair row (token t, slot k)
 // into the receive buffer of the rank that owns token t, over NVLink for other
 // ranks, instead of the local pair rows; the transfer overlaps the GEMM.  k is
@@ -55,7 +60,12 @@ constexpr int kOffA = kOffW + kConvStages * kWBytes;
 constexpr int kOffBar = kOffA + kAStages * kABytes;
 constexpr int kNumBars = 2 * kRawStages + 2 * kConvStages + 2 * kAStages + 4 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+// Epilogue staging: each epilogue warp's 32 rows x 64 columns (f16), rows padded
+// to 144 bytes so that both the row-per-lane writes and the 8-lanes-per-row reads
+// are free of bank conflicts.
+constexpr int kStageStride = 144;
+constexpr int kOffStage = (kOffMisc + 16 + 127) / 128 * 128;
+constexpr int kSmemBytes = kOffStage + 4 * 32 * kStageStride + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory over the per-CTA limit");
 
 struct Ring {
@@ -321,24 +331,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           drow = ps.base[o] + ((size_t)(t - o * ps.rows_per_rank) * kTopK + k) * kHidden;
         }
       }
-      uint4* dst = reinterpret_cast<uint4*>(drow + nt * kN);
+      drow += nt * kN;
+      uint8_t* stage = sm + kOffStage + q * 32 * kStageStride;
       bool sat = false;
-#pragma unroll 4
-      for (int c = 0; c < kN / 16; ++c) {
-        float p[16];
-        tmem_ld16(tmem_base + lane_base + buf * kN + 16 * c, p);
-        tmem_wait_ld();
-        const float f = c < 8 ? f_lo : f_hi;
-        uint32_t w[8];
+#pragma unroll 1
+      for (int g = 0; g < kN / 64; ++g) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const __half a = to_half_sat(p[2 * i] * f, sat), b = to_half_sat(p[2 * i + 1] * f, sat);
-          w[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * g + cc;
+          float p[16];
+          tmem_ld16(tmem_base + lane_base + buf * kN + 16 * c, p);
+          tmem_wait_ld();
+          const float f = c < 8 ? f_lo : f_hi;
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const __half a = to_half_sat(p[2 * i] * f, sat), b = to_half_sat(p[2 * i + 1] * f, sat);
+            w[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+          }
+          uint4* st = reinterpret_cast<uint4*>(stage + lane * kStageStride + cc * 32);
+          st[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          st[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
-        if (has_dst) {
-          dst[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int rr = 4 * j + (lane >> 3), ch = lane & 7;
+          __half* rp = reinterpret_cast<__half*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(drow), rr));
+          const int rd = __shfl_sync(0xffffffffu, has_dst ? 1 : 0, rr);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * kStageStride + ch * 16);
+          if (rd) *reinterpret_cast<uint4*>(rp + g * 64 + ch * 8) = v;
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
