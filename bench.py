@@ -212,7 +212,7 @@ def run_ours(args, world, rank, local):
     exchange = None
     if world > 1 and args.combine == "p2p":
         import fbmoe_ep
-        exchange = fbmoe_ep.PeerExchange(T_EP)
+        exchange = fbmoe_ep.PeerExchange(T_EP, dispatch=True)
     step, out = make_step(inp, world, rank, exchange)
     for _ in range(args.warmup):
         step()
@@ -257,6 +257,7 @@ def run_ours(args, world, rank, local):
                 "active_local_experts": active}
 
     e2e = run_e2e(args, world, rank, inp, E_local, off, exchange)
+    dispatch = run_dispatch(args, world, rank, inp, exchange) if exchange is not None else None
     if exchange is not None:
         exchange.close()
     combine = ("none" if world == 1 else "GEMM2 epilogue stores pair rows into the owner's buffer over NVLink "
@@ -274,6 +275,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": launches_per_forward(T_EP, E_local, world, exchange is not None) * args.steps,
         "clocks": clk.summary(),
     }
+    if dispatch is not None:
+        line["token_dispatch"] = dispatch
     if world == 1 and not args.no_sweep:
         line["decode_sweep"] = decode_sweep(peaks)
         line["quantiser"] = quantiser_point(peaks)
@@ -281,6 +284,37 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline_ep(inp, E_local, budget_s=args.cpu_budget)
     return line
+
+
+def run_dispatch(args, world, rank, inp, exchange):
+    """The token-dispatch layer on the same workload: rank r holds only tokens [r*T/N, (r+1)*T/N) (their logits,
+    fp8 rows and scales), routes them, ships rows to the experts' ranks and gets its tokens' output rows back
+    (csrc/moe_ep.cu).  Same T and experts as the replicated-input line; device time, max over ranks."""
+    import fbmoe_ep
+    lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
+    loc = (inp["routing_logits"][lo:hi].contiguous(), inp["routing_bias"], inp["hidden_states"][lo:hi].contiguous(),
+           inp["hidden_states_scale"][:, lo:hi].contiguous())
+    w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+    out = torch.empty((hi - lo, H), dtype=torch.bfloat16, device="cuda")
+
+    def step():
+        exchange.forward_dispatch(*loc, *w, inp["routed_scaling_factor"], out=out)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    s.record()
+    for _ in range(args.steps):
+        step()
+    e.record()
+    barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e), world)
+    status = exchange.status()
+    return {"value": round(T_EP * args.steps / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms / args.steps, 4),
+            "inputs": "token-sharded (each rank holds T/N tokens)", "status": status,
+            "gpu_launches_per_step": launches_per_forward(T_EP, E_TOTAL // world, world, True) + 3}
 
 
 def run_e2e(args, world, rank, inp, E_local, off, exchange=None):

@@ -120,6 +120,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
                  size_t workspace_bytes, void* stream, bool allow_split = true,
-                 const PeerScatter* scatter = nullptr);
+                 const PeerScatter* scatter = nullptr, const int32_t* routed_idx = nullptr,
+                 const float* routed_w = nullptr);
 
 }  // namespace fbmoe

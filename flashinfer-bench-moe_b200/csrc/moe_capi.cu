@@ -183,14 +183,18 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
-                 size_t workspace_bytes, void* stream_, bool allow_split, const PeerScatter* scatter) {
+                 size_t workspace_bytes, void* stream_, bool allow_split, const PeerScatter* scatter,
+                 const int32_t* routed_idx, const float* routed_w) {
   if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
   const bool scattering = scatter != nullptr && scatter->world > 0;
-  if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale || !gemm1_weights ||
+  // routed_idx / routed_w: routing computed elsewhere (token-dispatch expert parallelism); no router launch
+  const bool routed = routed_idx != nullptr;
+  if (routed && !routed_w) return FBMOE_ERR_NULL_POINTER;
+  if ((!routed && (!routing_logits || !routing_bias)) || !hidden_states || !hidden_states_scale || !gemm1_weights ||
       !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || (!out && !scattering) || !workspace)
     return FBMOE_ERR_NULL_POINTER;
-  if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
+  if ((!routed && (!aligned(routing_logits, 16) || !aligned(routing_bias, 16))) || !aligned(hidden_states, 16) ||
       !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(out, 16) || !aligned(workspace, 256))
     return FBMOE_ERR_MISALIGNED;
   // the scatter lives in the row-major GEMM2's epilogue, so it forces that chain
@@ -230,12 +234,15 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
     std::lock_guard<std::mutex> lk(g_prof.mu);
     if (g_prof.on && g_prof.n < g_prof.cap) fwd = g_prof.n++;
   }
-  int32_t* topk_idx = reinterpret_cast<int32_t*>(ws + L.topk_idx);
-  float* topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+  const int32_t* topk_idx = routed ? routed_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
+  const float* topk_w = routed ? routed_w : reinterpret_cast<float*>(ws + L.topk_w);
   prof_record(fwd, 0, stream);
-  cudaError_t e = launch_route(routing_logits, routing_bias, T, routed_scaling_factor, topk_idx, topk_w,
-                               reinterpret_cast<uint32_t*>(ws + L.status), stream);
-  if (e != cudaSuccess) return from_cuda(e);
+  cudaError_t e = cudaSuccess;
+  if (!routed) {
+    e = launch_route(routing_logits, routing_bias, T, routed_scaling_factor, reinterpret_cast<int32_t*>(ws + L.topk_idx),
+                     reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<uint32_t*>(ws + L.status), stream);
+    if (e != cudaSuccess) return from_cuda(e);
+  }
   prof_record(fwd, 1, stream);
   e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, sms, L, ws, stream);
   if (e != cudaSuccess) return from_cuda(e);

@@ -96,7 +96,8 @@ class PeerExchange:
     exchanged once (CUDA IPC handles over ``all_gather_object``); each ``forward``
     is one expert-parallel MoE layer with no NCCL call in the data path."""
 
-    def __init__(self, T: int, group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None):
+    def __init__(self, T: int, group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None,
+                 dispatch: bool = False):
         import fbmoe_lib
         self.lib = fbmoe_lib
         self.group = group
@@ -109,29 +110,58 @@ class PeerExchange:
         nbytes = fbmoe_lib.ep_recv_bytes(self.T, self.world)
         if nbytes == 0:
             raise ValueError(f"no receive buffer for T={T}, world={self.world}")
-        self.local = fbmoe_lib.ipc_alloc(nbytes)
-        handles: List[Optional[bytes]] = [None] * self.world
-        dist.all_gather_object(handles, fbmoe_lib.ipc_handle(self.local), group=group)
         self.opened: List[int] = []
-        ptrs = []
-        for o in range(self.world):
-            if o == self.rank:
-                ptrs.append(self.local)
-            else:
-                p = fbmoe_lib.ipc_open(handles[o])
-                self.opened.append(p)
-                ptrs.append(p)
-        self.ptrs: Sequence[int] = ptrs
+        self.local, self.ptrs = self._share(nbytes)
+        self.dispatch_local, self.dispatch_ptrs = 0, None
+        if dispatch:
+            self.dispatch_local, self.dispatch_ptrs = self._share(fbmoe_lib.ep_dispatch_bytes(self.T, self.world))
         self.workspace = torch.empty(fbmoe_lib.ep_workspace_size(self.T, self.E_local), dtype=torch.uint8,
                                      device=self.device)
         self.epoch = 0
         dist.barrier(group=group)  # every rank's buffer exists and is mapped before the first send
 
+    def _share(self, nbytes: int):
+        """Allocate this rank's buffer and map every peer's: (own address, addresses by rank)."""
+        local = self.lib.ipc_alloc(nbytes)
+        handles: List[Optional[bytes]] = [None] * self.world
+        dist.all_gather_object(handles, self.lib.ipc_handle(local), group=self.group)
+        ptrs = []
+        for o in range(self.world):
+            if o == self.rank:
+                ptrs.append(local)
+            else:
+                p = self.lib.ipc_open(handles[o])
+                self.opened.append(p)
+                ptrs.append(p)
+        return local, ptrs
+
+    def _next_epoch(self) -> int:
+        self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFF0 else 1
+        return self.epoch
+
+    def forward_dispatch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                         gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor,
+                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Token-dispatch layer: this rank passes only its own tokens (routing_logits [T/N, 256], hidden_states
+        [T/N, 7168], hidden_states_scale [56, T/N]) and its expert shard; returns its tokens' output rows."""
+        if self.dispatch_ptrs is None:
+            raise RuntimeError("PeerExchange was created without dispatch=True")
+        epoch = self._next_epoch()
+        if out is None:
+            out = torch.empty((self.T // self.world, H), dtype=torch.bfloat16, device=self.device)
+        self.lib.ep_dispatch_send(routing_logits, routing_bias, hidden_states, hidden_states_scale, self.T,
+                                  self.E_local, routed_scaling_factor, self.rank, self.world, self.dispatch_ptrs,
+                                  epoch, self.workspace)
+        self.lib.ep_dispatch_compute(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, self.T,
+                                     self.rank, self.world, self.dispatch_local, self.ptrs, epoch, self.workspace)
+        return self.lib.ep_recv(self.local, self.T, self.rank, self.world, epoch, out, self.workspace)
+
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor,
                 out: Optional[torch.Tensor] = None, check: bool = True) -> torch.Tensor:
-        """This rank's token rows [T/world, 7168] bf16 of the layer output (its expert shard's weights)."""
-        self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFF0 else 1
+        """This rank's token rows [T/world, 7168] bf16 of the layer output (its expert shard's weights); every
+        rank passes all T tokens' inputs (replicated)."""
+        self._next_epoch()
         if out is None:
             out = torch.empty((self.T // self.world, H), dtype=torch.bfloat16, device=self.device)
         inputs = (routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
@@ -150,6 +180,7 @@ class PeerExchange:
         for p in self.opened:
             self.lib.ipc_close(p)
         self.opened = []
-        if self.local:
-            self.lib.ipc_free(self.local)
-            self.local = 0
+        for attr in ("local", "dispatch_local"):
+            if getattr(self, attr):
+                self.lib.ipc_free(getattr(self, attr))
+                setattr(self, attr, 0)

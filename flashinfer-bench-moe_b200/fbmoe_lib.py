@@ -83,6 +83,16 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_forward_ep.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, i32, vp, u32, vp,
                                          vp, sz, vp]
         lib.fbmoe_forward_ep.restype = i32
+        lib.fbmoe_ep_dispatch_bytes.argtypes = [i32, i32]
+        lib.fbmoe_ep_dispatch_bytes.restype = sz
+        lib.fbmoe_forward_ep_dispatch_send.argtypes = [vp, vp, vp, vp, i32, i32, f32, i32, i32, vp, u32, vp, sz, vp]
+        lib.fbmoe_forward_ep_dispatch_send.restype = i32
+        lib.fbmoe_forward_ep_dispatch_compute.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, u32, vp, sz,
+                                                          vp]
+        lib.fbmoe_forward_ep_dispatch_compute.restype = i32
+        lib.fbmoe_forward_ep_dispatch.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, i32, i32, vp, vp, u32,
+                                                  vp, vp, sz, vp]
+        lib.fbmoe_forward_ep_dispatch.restype = i32
         lib.fbmoe_ipc_alloc.argtypes = [sz, ctypes.POINTER(vp)]
         lib.fbmoe_ipc_alloc.restype = i32
         lib.fbmoe_ipc_free.argtypes = [vp]
@@ -348,3 +358,39 @@ def ep_recv(my_ptr: int, T: int, rank: int, world: int, epoch: int, out: torch.T
     _check(load_library().fbmoe_forward_ep_recv(my_ptr, int(T), int(rank), int(world), int(epoch), out.data_ptr(),
                                                 workspace.data_ptr(), stream))
     return out
+
+
+def ep_dispatch_bytes(T: int, world: int) -> int:
+    """Bytes of one rank's token-dispatch buffer (0 if T % world != 0)."""
+    return int(load_library().fbmoe_ep_dispatch_bytes(int(T), int(world)))
+
+
+def ep_dispatch_send(logits_local, bias, hs_local, hs_scale_local, T: int, E_local: int, scale: float, rank: int,
+                     world: int, peer_dispatch, epoch: int, workspace: torch.Tensor) -> None:
+    """Route this rank's T/world tokens and write their routing (to every rank) and rows (to the ranks owning one
+    of their experts) into the peers' dispatch buffers, then flag the peers."""
+    T_r = T // world
+    _require(logits_local.is_cuda and logits_local.dtype == torch.float32 and logits_local.is_contiguous()
+             and tuple(logits_local.shape) == (T_r, E_GLOBAL), "routing_logits must be [T/world, 256] float32")
+    _require(hs_local.dtype == torch.float8_e4m3fn and hs_local.is_contiguous() and tuple(hs_local.shape) == (T_r, H),
+             "hidden_states must be [T/world, 7168] float8_e4m3fn")
+    _require(hs_scale_local.dtype == torch.float32 and hs_scale_local.is_contiguous()
+             and tuple(hs_scale_local.shape) == (H // 128, T_r), "hidden_states_scale must be [56, T/world]")
+    _require(bias.dtype == torch.bfloat16 and bias.numel() == E_GLOBAL, "routing_bias must be 256 bfloat16")
+    stream = torch.cuda.current_stream(hs_local.device).cuda_stream
+    _check(load_library().fbmoe_forward_ep_dispatch_send(
+        logits_local.data_ptr(), bias.data_ptr(), hs_local.data_ptr(), hs_scale_local.data_ptr(), int(T),
+        int(E_local), float(scale), int(rank), int(world), _ptr_array(peer_dispatch), int(epoch),
+        workspace.data_ptr(), int(workspace.numel()), stream))
+
+
+def ep_dispatch_compute(w1, s1, w2, s2, T: int, rank: int, world: int, my_dispatch: int, peer_recv, epoch: int,
+                        workspace: torch.Tensor) -> None:
+    """Wait for every rank's dispatch of ``epoch``, run this rank's experts over the dispatched tokens and store
+    the pair rows into their home ranks' receive buffers, then flag them."""
+    E = w1.size(0)
+    _require(tuple(w1.shape) == (E, 2 * I, H) and tuple(w2.shape) == (E, H, I), "bad expert weights")
+    stream = torch.cuda.current_stream(w1.device).cuda_stream
+    _check(load_library().fbmoe_forward_ep_dispatch_compute(
+        w1.data_ptr(), s1.data_ptr(), w2.data_ptr(), s2.data_ptr(), int(T), int(E), int(rank), int(world),
+        int(my_dispatch), _ptr_array(peer_recv), int(epoch), workspace.data_ptr(), int(workspace.numel()), stream))

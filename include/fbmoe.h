@@ -176,6 +176,40 @@ FBMOE_API int fbmoe_forward_ep(const float* routing_logits, const void* routing_
                                uint32_t epoch, void* out_rows_bf16, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/* ---- Token-dispatch expert parallelism: rank r holds only its own tokens
+ * [r*T/world, (r+1)*T/world) -- routing_logits [T/world, 256], hidden_states
+ * [T/world, 7168] e4m3, hidden_states_scale [56, T/world] -- and experts
+ * [r*E_local, (r+1)*E_local), E_local*world == 256.  T is the global token count.
+ * _send routes the rank's tokens and writes each token's top-8 into every rank's
+ * dispatch buffer and its row and scales into the ranks that own one of its
+ * experts (peer_dispatch[o]: rank o's fbmoe_ep_dispatch_bytes buffer), then flags
+ * every peer.  _compute waits (bounded, status bit 7) for every rank's dispatch of
+ * `epoch` and runs permute .. GEMM2 on this rank's experts over the global token
+ * space, GEMM2 storing pair rows into the home ranks' receive buffers (peer_recv,
+ * as for fbmoe_forward_ep_send), then flags them.  fbmoe_forward_ep_recv then
+ * gives this rank's tokens' output rows -- equal, bit for bit, to fbmoe_forward
+ * with all 256 experts on all T tokens.  fbmoe_forward_ep_dispatch = the three in
+ * order.  Workspace: fbmoe_ep_workspace_size(T, E_local). */
+FBMOE_API size_t fbmoe_ep_dispatch_bytes(int T, int world);
+FBMOE_API int fbmoe_forward_ep_dispatch_send(const float* routing_logits, const void* routing_bias,
+                                             const void* hidden_states, const float* hidden_states_scale, int T,
+                                             int E_local, float routed_scaling_factor, int rank, int world,
+                                             void* const* peer_dispatch, uint32_t epoch, void* workspace,
+                                             size_t workspace_bytes, void* stream);
+FBMOE_API int fbmoe_forward_ep_dispatch_compute(const void* gemm1_weights, const float* gemm1_weights_scale,
+                                                const void* gemm2_weights, const float* gemm2_weights_scale, int T,
+                                                int E_local, int rank, int world, void* my_dispatch,
+                                                void* const* peer_recv, uint32_t epoch, void* workspace,
+                                                size_t workspace_bytes, void* stream);
+FBMOE_API int fbmoe_forward_ep_dispatch(const float* routing_logits, const void* routing_bias,
+                                        const void* hidden_states, const float* hidden_states_scale,
+                                        const void* gemm1_weights, const float* gemm1_weights_scale,
+                                        const void* gemm2_weights, const float* gemm2_weights_scale, int T,
+                                        int E_local, float routed_scaling_factor, int rank, int world,
+                                        void* const* peer_dispatch, void* const* peer_recv, uint32_t epoch,
+                                        void* out_rows_bf16, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* Device buffers shared across processes (cudaMalloc + CUDA IPC).  A handle is
  * FBMOE_IPC_HANDLE_BYTES opaque bytes; open it in every other process of the node. */
 #define FBMOE_IPC_HANDLE_BYTES 64

@@ -1,6 +1,7 @@
 """Expert parallelism over CUDA-IPC peer memory, one process per GPU (needs 2 or more
 GPUs; skipped otherwise).  Each rank checks its token rows against the single-GPU
-operator with all 256 experts, bit for bit, over three consecutive calls."""
+operator with all 256 experts, bit for bit, over three consecutive calls of the
+replicated-input layer and three of the token-dispatch layer."""
 import os
 import socket
 import sys
@@ -35,7 +36,7 @@ def _rank_main(rank, world, port, q):
         import fbmoe_workloads as W
         L.load_library()
         w1, s1, w2, s2 = W.make_weights(256, 777, "cuda")
-        ex = fbmoe_ep.PeerExchange(T)
+        ex = fbmoe_ep.PeerExchange(T, dispatch=True)
         E, off = ex.E_local, ex.offset
         lo, hi = fbmoe_ep.row_range(rank, world, T)
         ok, msg = True, ""
@@ -49,6 +50,14 @@ def _rank_main(rank, world, port, q):
             same = torch.equal(out.view(torch.int16), ref[lo:hi].view(torch.int16))
             if st != 0 or not same:
                 ok, msg = False, f"{config}: status {st}, equal {same}"
+            out = ex.forward_dispatch(inp["routing_logits"][lo:hi].contiguous(), inp["routing_bias"],
+                                      inp["hidden_states"][lo:hi].contiguous(),
+                                      inp["hidden_states_scale"][:, lo:hi].contiguous(), w1[off:off + E],
+                                      s1[off:off + E], w2[off:off + E], s2[off:off + E], inp["routed_scaling_factor"])
+            st = ex.status()
+            same = torch.equal(out.view(torch.int16), ref[lo:hi].view(torch.int16))
+            if st != 0 or not same:
+                ok, msg = False, f"dispatch {config}: status {st}, equal {same}"
         ex.close()
         dist.destroy_process_group()
         q.put((rank, ok, msg))

@@ -127,3 +127,50 @@ def test_ep_recv_times_out_when_a_peer_never_sends(fbmoe_lib, workloads, weights
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
     finally:
         ranks.close()
+
+
+class EmulatedDispatch(EmulatedRanks):
+    """Token-dispatch ranks on one GPU: rank r passes only tokens [r*T/N, (r+1)*T/N).
+    All dispatches, then all computes, then all receives."""
+
+    def __init__(self, lib, T, world):
+        super().__init__(lib, T, world)
+        self.dbufs = [lib.ipc_alloc(lib.ep_dispatch_bytes(T, world)) for _ in range(world)]
+
+    def local_inputs(self, inp, r):
+        n = self.T // self.world
+        lo, hi = r * n, (r + 1) * n
+        return (inp["routing_logits"][lo:hi].contiguous(), inp["routing_bias"], inp["hidden_states"][lo:hi].contiguous(),
+                inp["hidden_states_scale"][:, lo:hi].contiguous())
+
+    def forward(self, inp, epoch):
+        for r in range(self.world):
+            logits, bias, hs, hss = self.local_inputs(inp, r)
+            self.lib.ep_dispatch_send(logits, bias, hs, hss, self.T, self.E, inp["routed_scaling_factor"], r,
+                                      self.world, self.dbufs, epoch, self.ws[r])
+        for r in range(self.world):
+            lo, hi = r * self.E, (r + 1) * self.E
+            self.lib.ep_dispatch_compute(inp["gemm1_weights"][lo:hi], inp["gemm1_weights_scale"][lo:hi],
+                                         inp["gemm2_weights"][lo:hi], inp["gemm2_weights_scale"][lo:hi], self.T, r,
+                                         self.world, self.dbufs[r], self.bufs, epoch, self.ws[r])
+        return torch.cat([self.recv(r, epoch) for r in range(self.world)], dim=0)
+
+    def close(self):
+        super().close()
+        for b in self.dbufs:
+            self.lib.ipc_free(b)
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_token_dispatch_equals_single_gpu_bit_for_bit(fbmoe_lib, workloads, weights256, world):
+    T = 256
+    ranks = EmulatedDispatch(fbmoe_lib, T, world)
+    try:
+        for epoch, (seed, config) in enumerate([(21, "standard"), (22, "group"), (23, "skew")], start=1):
+            inp = _inputs(workloads, weights256, T, seed=seed, config=config)
+            ref = _single_gpu(fbmoe_lib, workloads, inp)
+            out = ranks.forward(inp, epoch=epoch)
+            assert ranks.statuses() == [0] * world, (world, config)
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), (world, config)
+    finally:
+        ranks.close()
