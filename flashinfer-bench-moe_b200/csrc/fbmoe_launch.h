@@ -87,6 +87,11 @@ cudaError_t launch_route(const float* logits, const void* bias_bf16, int T, floa
 
 // Histogram / padded offsets / deterministic permutation / GEMM block list.
 // Also zeroes the decode kernel's arrival counters.
+// Router + permutation in one CTA for 1 <= T <= 16 (the decode path): the same
+// workspace outputs as launch_route followed by launch_permute.
+cudaError_t launch_route_permute_small(const float* logits, const void* bias_bf16, int T, float scale, int E_local,
+                                       int local_offset, int bn, const Layout& L, uint8_t* ws, cudaStream_t stream);
+
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
                            int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream);
 

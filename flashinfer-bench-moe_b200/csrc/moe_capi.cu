@@ -238,14 +238,23 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   const float* topk_w = routed ? routed_w : reinterpret_cast<float*>(ws + L.topk_w);
   prof_record(fwd, 0, stream);
   cudaError_t e = cudaSuccess;
-  if (!routed) {
-    e = launch_route(routing_logits, routing_bias, T, routed_scaling_factor, reinterpret_cast<int32_t*>(ws + L.topk_idx),
-                     reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<uint32_t*>(ws + L.status), stream);
+  if (!routed && bn == 16 && T <= 16) {
+    // decode: router and permutation in one CTA (its time is the "route" stage of the profile)
+    e = launch_route_permute_small(routing_logits, routing_bias, T, routed_scaling_factor, E_local,
+                                   local_expert_offset, bn, L, ws, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    prof_record(fwd, 1, stream);
+  } else {
+    if (!routed) {
+      e = launch_route(routing_logits, routing_bias, T, routed_scaling_factor,
+                       reinterpret_cast<int32_t*>(ws + L.topk_idx), reinterpret_cast<float*>(ws + L.topk_w),
+                       reinterpret_cast<uint32_t*>(ws + L.status), stream);
+      if (e != cudaSuccess) return from_cuda(e);
+    }
+    prof_record(fwd, 1, stream);
+    e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, sms, L, ws, stream);
     if (e != cudaSuccess) return from_cuda(e);
   }
-  prof_record(fwd, 1, stream);
-  e = launch_permute(topk_idx, topk_w, T, E_local, local_expert_offset, bn, sms, L, ws, stream);
-  if (e != cudaSuccess) return from_cuda(e);
   prof_record(fwd, 2, stream);
   if (bn == 16) {
     // decode: GEMM1, GEMM2 and the combine run as one kernel (its time is the

@@ -24,8 +24,13 @@
 // the block list.  Within a chunk, a token's rank inside an expert is the number
 // of set bits before it in that expert's 1024-bit membership mask, which is
 // order-independent.
+//
+// Up to 16 tokens (route_permute_small_kernel): one CTA of 16 warps routes the
+// tokens (a warp each, moe_route.cuh) and then permutes them, one launch instead
+// of two; its top-8 goes to the workspace as the router kernel's does.
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
+#include "moe_route.cuh"
 
 namespace fbmoe {
 namespace {
@@ -236,7 +241,9 @@ __global__ void __launch_bounds__(kThreads) permute_kernel(const int32_t* __rest
 constexpr int kSmallT = 64;
 constexpr int kSmallThreads = kSmallT * kTopK;  // 512
 
-__global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
+// The small permutation, run by all 512 threads of the calling CTA.  topk_idx /
+// topk_w are read through L2 (they may have been written by this CTA moments before).
+__device__ __forceinline__ void permute_small_body(
     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, int T, int E_local, int local_offset,
     int bn, int32_t* __restrict__ expert_cnt, int32_t* __restrict__ expert_poff, int32_t* __restrict__ n_blocks,
     int4* __restrict__ blocks, int max_blocks, int32_t* __restrict__ row_token, float* __restrict__ row_weight,
@@ -249,8 +256,6 @@ __global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
   __shared__ int wsum[2][kMaxLocal / 32];
   __shared__ int nblk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_wait();
-  pdl_trigger();
   if (tid < kMaxLocal) {
     cnt[tid] = 0;
     mask[tid] = 0ull;
@@ -259,7 +264,7 @@ __global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
   const int t = tid / kTopK;
   int e = -1;
   if (t < T) {
-    e = topk_idx[tid] - local_offset;
+    e = __ldcg(topk_idx + tid) - local_offset;
     if ((unsigned)e < (unsigned)E_local) {
       atomicAdd(&cnt[e], 1);
       atomicOr(&mask[e], 1ull << t);
@@ -329,13 +334,85 @@ __global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
     if (e >= 0) {
       row = poff[e] + __popcll(mask[e] & ((1ull << t) - 1ull));
       row_token[row] = t;
-      row_weight[row] = topk_w[tid];
+      row_weight[row] = __ldcg(topk_w + tid);
     }
     token_rows[tid] = row;
   }
 }
 
+__global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
+    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, int T, int E_local, int local_offset,
+    int bn, int32_t* __restrict__ expert_cnt, int32_t* __restrict__ expert_poff, int32_t* __restrict__ n_blocks,
+    int4* __restrict__ blocks, int max_blocks, int32_t* __restrict__ row_token, float* __restrict__ row_weight,
+    int32_t* __restrict__ token_rows, uint32_t* __restrict__ status, int32_t* __restrict__ splits,
+    int32_t* __restrict__ split_count, int split_items, int32_t* __restrict__ blk_ready,
+    int32_t* __restrict__ grid_sync) {
+  pdl_wait();
+  pdl_trigger();
+  permute_small_body(topk_idx, topk_w, T, E_local, local_offset, bn, expert_cnt, expert_poff, n_blocks, blocks,
+                     max_blocks, row_token, row_weight, token_rows, status, splits, split_count, split_items,
+                     blk_ready, grid_sync);
+}
+
+constexpr int kFusedT = kSmallThreads / 32;  // 16 tokens, a warp each
+
+// Router + small permutation for T <= 16 in one CTA.  Dynamic shared memory:
+// the router's per-warp scratch (256 values, 256 ids, 256 scores, 8 picks).
+__global__ void __launch_bounds__(kSmallThreads) route_permute_small_kernel(
+    const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, float scale,
+    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int T, int E_local, int local_offset,
+    int bn, int32_t* __restrict__ expert_cnt, int32_t* __restrict__ expert_poff, int32_t* __restrict__ n_blocks,
+    int4* __restrict__ blocks, int max_blocks, int32_t* __restrict__ row_token, float* __restrict__ row_weight,
+    int32_t* __restrict__ token_rows, uint32_t* __restrict__ status, int32_t* __restrict__ splits,
+    int32_t* __restrict__ split_count, int split_items, int32_t* __restrict__ blk_ready,
+    int32_t* __restrict__ grid_sync) {
+  extern __shared__ float route_scratch[];
+  const int warp = threadIdx.x >> 5;
+  float* wv = route_scratch + (size_t)warp * (3 * kExperts + kTopK);
+  int* wi = reinterpret_cast<int*>(wv + kExperts);
+  float* wsc = wv + 2 * kExperts;
+  int* wsel = reinterpret_cast<int*>(wv + 3 * kExperts);
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) status[0] = 0u;
+  const int t = warp;
+  float x[8];
+  if (t < T) route_dev::load_logits8(logits, t, x);
+  float bs[8];
+  route_dev::load_bias8(bias, bs);
+  if (t < T) route_dev::route_token(x, t, bs, scale, topk_idx, topk_w, wv, wi, wsc, wsel);
+  __threadfence_block();
+  __syncthreads();
+  permute_small_body(topk_idx, topk_w, T, E_local, local_offset, bn, expert_cnt, expert_poff, n_blocks, blocks,
+                     max_blocks, row_token, row_weight, token_rows, status, splits, split_count, split_items,
+                     blk_ready, grid_sync);
+}
+constexpr int kFusedSmem = kFusedT * (3 * kExperts + kTopK) * 4;
+
 }  // namespace
+
+cudaError_t launch_route_permute_small(const float* logits, const void* bias_bf16, int T, float scale, int E_local,
+                                       int local_offset, int bn, const Layout& L, uint8_t* ws, cudaStream_t stream) {
+  if (T < 1 || T > kFusedT) return cudaErrorInvalidValue;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(route_permute_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kFusedSmem);
+    if (err != cudaSuccess) return err;
+    attr_set[dev] = true;
+  }
+  return launch_pdl(route_permute_small_kernel, dim3(1), dim3(kSmallThreads), kFusedSmem, stream, logits,
+      reinterpret_cast<const __nv_bfloat16*>(bias_bf16), scale, reinterpret_cast<int32_t*>(ws + L.topk_idx),
+      reinterpret_cast<float*>(ws + L.topk_w), T, E_local, local_offset, bn,
+      reinterpret_cast<int32_t*>(ws + L.expert_cnt), reinterpret_cast<int32_t*>(ws + L.expert_poff),
+      reinterpret_cast<int32_t*>(ws + L.n_blocks), reinterpret_cast<int4*>(ws + L.blocks), L.max_blocks,
+      reinterpret_cast<int32_t*>(ws + L.row_token), reinterpret_cast<float*>(ws + L.row_weight),
+      reinterpret_cast<int32_t*>(ws + L.token_rows), reinterpret_cast<uint32_t*>(ws + L.status),
+      reinterpret_cast<int32_t*>(ws + L.splits), reinterpret_cast<int32_t*>(ws + L.split_count), L.split_items,
+      reinterpret_cast<int32_t*>(ws + L.blk_ready), reinterpret_cast<int32_t*>(ws + L.grid_sync));
+}
 
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
                            int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream) {
