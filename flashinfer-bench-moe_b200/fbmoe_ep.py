@@ -111,29 +111,70 @@ class PeerExchange:
         if nbytes == 0:
             raise ValueError(f"no receive buffer for T={T}, world={self.world}")
         self.opened: List[int] = []
-        self.local, self.ptrs = self._share(nbytes)
-        self.dispatch_local, self.dispatch_ptrs = 0, None
+        self.local, self.dispatch_local, self.dispatch_ptrs = 0, 0, None
+        # Set-up succeeds on every rank or fails on every rank with the same error: local steps
+        # are caught, the collectives always run, and the ranks exchange their errors.
+        self.local, self.ptrs, err = self._share(nbytes, None)
         if dispatch:
-            self.dispatch_local, self.dispatch_ptrs = self._share(fbmoe_lib.ep_dispatch_bytes(self.T, self.world))
-        self.workspace = torch.empty(fbmoe_lib.ep_workspace_size(self.T, self.E_local), dtype=torch.uint8,
-                                     device=self.device)
+            self.dispatch_local, self.dispatch_ptrs, err = self._share(
+                fbmoe_lib.ep_dispatch_bytes(self.T, self.world), err)
+        self.workspace = None
+        if err is None:
+            try:
+                self.workspace = torch.empty(fbmoe_lib.ep_workspace_size(self.T, self.E_local), dtype=torch.uint8,
+                                             device=self.device)
+            except Exception as e:  # reported collectively below
+                err = f"workspace: {e!r}"
+        errors: List[Optional[str]] = [None] * self.world
+        dist.all_gather_object(errors, err, group=group)
+        failed = [(r, e) for r, e in enumerate(errors) if e is not None]
+        if failed:
+            self._release()
+            raise RuntimeError("peer exchange unavailable: " + "; ".join(f"rank {r}: {e}" for r, e in failed))
         self.epoch = 0
         dist.barrier(group=group)  # every rank's buffer exists and is mapped before the first send
 
-    def _share(self, nbytes: int):
-        """Allocate this rank's buffer and map every peer's: (own address, addresses by rank)."""
-        local = self.lib.ipc_alloc(nbytes)
+    def _share(self, nbytes: int, err: Optional[str]):
+        """Allocate this rank's buffer and map every peer's: (own address, addresses by rank, error or None).
+        The handle exchange runs on every rank whatever happened locally."""
+        local, handle, ptrs = 0, None, []
+        if err is None:
+            try:
+                local = self.lib.ipc_alloc(nbytes)
+                handle = self.lib.ipc_handle(local)
+            except Exception as e:
+                err = f"allocation: {e!r}"
         handles: List[Optional[bytes]] = [None] * self.world
-        dist.all_gather_object(handles, self.lib.ipc_handle(local), group=self.group)
-        ptrs = []
-        for o in range(self.world):
-            if o == self.rank:
-                ptrs.append(local)
-            else:
-                p = self.lib.ipc_open(handles[o])
-                self.opened.append(p)
-                ptrs.append(p)
-        return local, ptrs
+        dist.all_gather_object(handles, handle, group=self.group)
+        if err is None:
+            try:
+                for o in range(self.world):
+                    if o == self.rank:
+                        ptrs.append(local)
+                    elif handles[o] is None:
+                        raise RuntimeError(f"rank {o} has no buffer")
+                    else:
+                        p = self.lib.ipc_open(handles[o])
+                        self.opened.append(p)
+                        ptrs.append(p)
+            except Exception as e:
+                err = f"mapping: {e!r}"
+        return local, ptrs, err
+
+    def _release(self) -> None:
+        for p in self.opened:
+            try:
+                self.lib.ipc_close(p)
+            except Exception:
+                pass
+        self.opened = []
+        for attr in ("local", "dispatch_local"):
+            if getattr(self, attr, 0):
+                try:
+                    self.lib.ipc_free(getattr(self, attr))
+                except Exception:
+                    pass
+                setattr(self, attr, 0)
 
     def _next_epoch(self) -> int:
         self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFF0 else 1
@@ -177,10 +218,4 @@ class PeerExchange:
         """Unmap the peers' buffers and free this rank's (collective: call on every rank)."""
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # no peer still writes into this rank's buffer
-        for p in self.opened:
-            self.lib.ipc_close(p)
-        self.opened = []
-        for attr in ("local", "dispatch_local"):
-            if getattr(self, attr):
-                self.lib.ipc_free(getattr(self, attr))
-                setattr(self, attr, 0)
+        self._release()

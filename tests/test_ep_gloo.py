@@ -105,3 +105,40 @@ def test_ep_combine_and_shard_equivalence_gloo(oracle_mod):
     combined = torch.cat([got[r][1] for r in range(world)])
     st = oracle_mod.error_stats(combined, full, ATOL, RTOL)
     assert st["frac_pass"] == 1.0 and st["max_abs"] <= 1e-2, st
+
+
+def _exchange_rank(rank, world, port, q):
+    import sys
+    sys.path.insert(0, PKG)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import fbmoe_ep
+        import fbmoe_lib
+        fbmoe_lib.load_library()
+        try:
+            fbmoe_ep.PeerExchange(8, device=torch.device("cpu"))
+            q.put((rank, "constructed"))
+        except RuntimeError as e:
+            q.put((rank, str(e)))
+        dist.barrier()  # the ranks are still in step after the failure
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_setup_fails_on_every_rank_alike(fbmoe_lib):
+    """Without a GPU the receive buffers cannot be allocated: every rank must raise the same error
+    (none may be left waiting in a collective), so a caller can fall back on all ranks together."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0] == got[1] and got[0].startswith("peer exchange unavailable")
+    assert "rank 0" in got[0] and "rank 1" in got[0]

@@ -1,5 +1,5 @@
-"""Expert parallelism over CUDA-IPC peer memory, one process per GPU (needs 2 or more
-GPUs; skipped otherwise).  Each rank checks its token rows against the single-GPU
+"""Expert parallelism over CUDA-IPC peer memory, one process per GPU (2 or 4 ranks when
+the box has that many GPUs; on one GPU a single rank still runs the whole host path).  Each rank checks its token rows against the single-GPU
 operator with all 256 experts, bit for bit, over three consecutive calls of the
 replicated-input layer and three of the token-dispatch layer."""
 import os
@@ -65,10 +65,10 @@ def _rank_main(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_over_peer_memory_matches_single_gpu():
     import torch.multiprocessing as mp
-    world = 2 if torch.cuda.device_count() < 4 else 4
+    n = torch.cuda.device_count()
+    world = 4 if n >= 4 else (2 if n >= 2 else 1)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
