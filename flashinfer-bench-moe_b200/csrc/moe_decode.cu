@@ -760,7 +760,7 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volat
   // consecutive tasks go to different CTAs, so a small T still uses many SMs
   const int first = threadIdx.x * gridDim.x + blockIdx.x;
   // A task's slot rows and plane counts depend only on the permutation, so the
-  // first task's are fetched before the grid arrival completes.
+  // first task's are fetched while the grid arrival completes.
   int rows[kTopK], np[kTopK];
   auto prep = [&](int task) {
     const int t = task / kGroupsPerRow, h = (task % kGroupsPerRow) * 8 / 128;
@@ -772,11 +772,13 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volat
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + h) : 0;
   };
-  if (first < tasks) prep(first);
-
   if (threadIdx.x == 0) {
     __threadfence();  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
     atomicAdd(a.grid_sync, 1);
+  }
+  // the first task's slot rows load while the other CTAs arrive
+  if (first < tasks) prep(first);
+  if (threadIdx.x == 0) {
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire_gpu(a.grid_sync) < (int)gridDim.x) {
       if (globaltimer_ns() - t0 > kWaitBudgetNs) {
