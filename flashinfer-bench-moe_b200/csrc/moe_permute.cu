@@ -242,7 +242,9 @@ constexpr int kSmallT = 64;
 constexpr int kSmallThreads = kSmallT * kTopK;  // 512
 
 // The small permutation, run by all 512 threads of the calling CTA.  topk_idx /
-// topk_w are read through L2 (they may have been written by this CTA moments before).
+// topk_w: global arrays written by an earlier kernel (read through L2), or, with
+// kLocalTopk, this CTA's shared-memory copy.
+template <bool kLocalTopk>
 __device__ __forceinline__ void permute_small_body(
     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, int T, int E_local, int local_offset,
     int bn, int32_t* __restrict__ expert_cnt, int32_t* __restrict__ expert_poff, int32_t* __restrict__ n_blocks,
@@ -264,7 +266,7 @@ __device__ __forceinline__ void permute_small_body(
   const int t = tid / kTopK;
   int e = -1;
   if (t < T) {
-    e = __ldcg(topk_idx + tid) - local_offset;
+    e = (kLocalTopk ? topk_idx[tid] : __ldcg(topk_idx + tid)) - local_offset;
     if ((unsigned)e < (unsigned)E_local) {
       atomicAdd(&cnt[e], 1);
       atomicOr(&mask[e], 1ull << t);
@@ -334,7 +336,7 @@ __device__ __forceinline__ void permute_small_body(
     if (e >= 0) {
       row = poff[e] + __popcll(mask[e] & ((1ull << t) - 1ull));
       row_token[row] = t;
-      row_weight[row] = __ldcg(topk_w + tid);
+      row_weight[row] = kLocalTopk ? topk_w[tid] : __ldcg(topk_w + tid);
     }
     token_rows[tid] = row;
   }
@@ -349,14 +351,15 @@ __global__ void __launch_bounds__(kSmallThreads) permute_small_kernel(
     int32_t* __restrict__ grid_sync) {
   pdl_wait();
   pdl_trigger();
-  permute_small_body(topk_idx, topk_w, T, E_local, local_offset, bn, expert_cnt, expert_poff, n_blocks, blocks,
+  permute_small_body<false>(topk_idx, topk_w, T, E_local, local_offset, bn, expert_cnt, expert_poff, n_blocks, blocks,
                      max_blocks, row_token, row_weight, token_rows, status, splits, split_count, split_items,
                      blk_ready, grid_sync);
 }
 
 constexpr int kFusedT = kSmallThreads / 32;  // 16 tokens, a warp each
 
-// Router + small permutation for T <= 16 in one CTA.  Dynamic shared memory:
+// Router + small permutation for T <= 16 in one CTA; the routing result stays in
+// shared memory between the two (no round trip through L2).  Dynamic shared memory:
 // the router's per-warp scratch (256 values, 256 ids, 256 scores, 8 picks).
 __global__ void __launch_bounds__(kSmallThreads) route_permute_small_kernel(
     const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, float scale,
@@ -367,6 +370,8 @@ __global__ void __launch_bounds__(kSmallThreads) route_permute_small_kernel(
     int32_t* __restrict__ split_count, int split_items, int32_t* __restrict__ blk_ready,
     int32_t* __restrict__ grid_sync) {
   extern __shared__ float route_scratch[];
+  __shared__ int s_idx[kFusedT * kTopK];
+  __shared__ float s_w[kFusedT * kTopK];
   const int warp = threadIdx.x >> 5;
   float* wv = route_scratch + (size_t)warp * (3 * kExperts + kTopK);
   int* wi = reinterpret_cast<int*>(wv + kExperts);
@@ -380,10 +385,14 @@ __global__ void __launch_bounds__(kSmallThreads) route_permute_small_kernel(
   if (t < T) route_dev::load_logits8(logits, t, x);
   float bs[8];
   route_dev::load_bias8(bias, bs);
-  if (t < T) route_dev::route_token(x, t, bs, scale, topk_idx, topk_w, wv, wi, wsc, wsel);
-  __threadfence_block();
+  // the top-8 stays in shared memory for the permutation; the workspace gets a copy
+  if (t < T) route_dev::route_token(x, t, bs, scale, s_idx, s_w, wv, wi, wsc, wsel);
   __syncthreads();
-  permute_small_body(topk_idx, topk_w, T, E_local, local_offset, bn, expert_cnt, expert_poff, n_blocks, blocks,
+  if ((int)threadIdx.x < T * kTopK) {
+    topk_idx[threadIdx.x] = s_idx[threadIdx.x];
+    topk_w[threadIdx.x] = s_w[threadIdx.x];
+  }
+  permute_small_body<true>(s_idx, s_w, T, E_local, local_offset, bn, expert_cnt, expert_poff, n_blocks, blocks,
                      max_blocks, row_token, row_weight, token_rows, status, splits, split_count, split_items,
                      blk_ready, grid_sync);
 }
