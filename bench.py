@@ -12,6 +12,8 @@ un-rounded fp32 partials.  At N = 1 the step is the plain fused_moe call.
 value  = tokens/s of the whole job (T * steps / max-over-ranks device time).
 e2e    = the same through the public API with the activations copied from pinned
          host memory and the rank's output rows copied back, inside the timing.
+At N > 1 the line's `token_dispatch` object (inputs token-sharded: each rank holds
+T/N tokens) carries its own `e2e`, in which each rank uploads only its tokens.
 On N = 1 the line also carries the decode sweep (config 1: T = 1..64, 32 local
 experts, HBM roofline) and prefill points (config 2: skewed routing, FP8 tensor
 roofline), each measured with L2 flushed between calls, after a 5 s idle pause
@@ -266,6 +268,8 @@ def run_ours(args, world, rank, local):
 
     e2e = run_e2e(args, world, rank, inp, E_local, off, exchange)
     dispatch = run_dispatch(args, world, rank, inp, exchange) if exchange is not None else None
+    if dispatch is not None:
+        dispatch["e2e"] = run_e2e(args, world, rank, inp, E_local, off, exchange, dispatch=True)
     if fallback is not None:
         dispatch = {"unavailable": fallback}
     if exchange is not None:
@@ -332,16 +336,24 @@ def run_dispatch(args, world, rank, inp, exchange):
             "gpu_launches_per_step": launches_per_forward(T_EP, E_TOTAL // world, world, True) + 3}
 
 
-def run_e2e(args, world, rank, inp, E_local, off, exchange=None):
+def run_e2e(args, world, rank, inp, E_local, off, exchange=None, dispatch=False):
     """Public API with host buffers: every step copies its activations H2D from pinned memory, runs fused_moe
     (+ the EP combine) and copies this rank's output rows D2H.  Steps are pipelined the way a server would run
     them: two device buffer sets, H2D on one copy stream and D2H on another, so step i+1's upload and step i-1's
     download overlap step i's compute (PCIe is full duplex).  Timed on the compute stream from before the first
-    upload to after the last download."""
+    upload to after the last download.  dispatch=True: the token-dispatch layer, each rank uploading only its own
+    tokens' logits, fp8 rows and scales."""
     import fbmoe_lib as L
     names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
-    host = {k: inp[k].cpu().pin_memory() for k in names}
-    dev = [{k: torch.empty_like(inp[k]) for k in names} for _ in range(2)]
+    if dispatch:
+        import fbmoe_ep
+        lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
+        src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
+               "hidden_states": inp["hidden_states"][lo:hi], "hidden_states_scale": inp["hidden_states_scale"][:, lo:hi]}
+    else:
+        src = {k: inp[k] for k in names}
+    host = {k: src[k].cpu().contiguous().pin_memory() for k in names}
+    dev = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device="cuda") for k in names} for _ in range(2)]
     w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
     rows = T_EP // world
     out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
@@ -371,7 +383,10 @@ def run_e2e(args, world, rank, inp, E_local, off, exchange=None):
         main.wait_event(ev_in[b])
         main.wait_event(ev_out[b])
         d = dev[b]
-        if world == 1:
+        if dispatch:
+            exchange.forward_dispatch(d["routing_logits"], d["routing_bias"], d["hidden_states"],
+                                      d["hidden_states_scale"], *w, inp["routed_scaling_factor"], out=out_dev[b])
+        elif world == 1:
             L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w, off,
                       inp["routed_scaling_factor"], out=out_dev[b])
         elif exchange is not None:
