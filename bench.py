@@ -34,6 +34,7 @@ import subprocess
 import sys
 import time
 
+import numpy as np
 import torch
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -161,6 +162,17 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+METRIC = "tokens/s per MoE layer call (DS-V3 FP8 MoE, T=8192, 256 experts, EP over N GPUs)"
+
+
+def workload_config(world):
+    """The workload both arms report (identical dicts): what one step computes, not how."""
+    E_local = E_TOTAL // world
+    return {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
+            "parallelism": f"ep{world}",
+            "l2": "inputs larger than L2 (weights %.1f GB per GPU)" % (E_local * BYTES_PER_EXPERT / 1e9)}
+
+
 # --------------------------------------------------------------------------- our arm
 def ep_inputs(world, rank):
     import fbmoe_ep
@@ -277,14 +289,12 @@ def run_ours(args, world, rank, local):
     combine = ("none" if world == 1 else "GEMM2 epilogue stores pair rows into the owner's buffer over NVLink "
                "(CUDA IPC), owner sums slots" if exchange is not None else "nccl reduce_scatter fp32")
     line = {
-        "metric": "tokens/s per MoE layer call (DS-V3 FP8 MoE, T=8192, 256 experts, EP over N GPUs)",
+        "metric": METRIC,
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp8_e4m3 GEMM1 / f16 GEMM2, fp32 accumulate",
         "data": "synthetic (seeded N(0,1) activations/logits, N(0,0.02) weights, FP8 block-quantised)",
-        "config": {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
-                   "parallelism": f"ep{world}", "combine": combine,
-                   "l2": "inputs larger than L2 (weights %.1f GB per GPU)" % (E_local * BYTES_PER_EXPERT / 1e9)},
+        "config": workload_config(world), "combine": combine,
         "roofline": roofline, "e2e": e2e,
         "gpu_launches": launches_per_forward(T_EP, E_local, world, exchange is not None) * args.steps,
         "clocks": clk.summary(),
@@ -301,7 +311,7 @@ def run_ours(args, world, rank, local):
                 line[key] = fn(peaks)
             line[key]["clocks"] = sweep_clk.summary()
     if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline_ep(inp, E_local, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = cpu_baseline_ep(inp, E_local)
     return line
 
 
@@ -517,80 +527,70 @@ def prefill_points(peaks):
 
 
 # --------------------------------------------------------------------------- CPU baselines
-def cpu_baseline_ep(inp, E_local, budget_s=20.0, n_exp=4):
-    cores = torch.get_num_threads()
-    keys = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
-    cpu = {k: inp[k].cpu() for k in keys}
-    cpu["local_expert_offset"] = inp["local_expert_offset"]
-    cpu["routed_scaling_factor"] = inp["routed_scaling_factor"]
-    est, spent, samples = [], 0.0, 0
-    e0 = 0
-    while spent < budget_s and samples < 8:
-        for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale"):
-            cpu[k] = inp[k][e0:e0 + n_exp].cpu()
-        full, used = _sample_block(cpu, inp, e0, n_exp, E_local)
-        est.append(full)
-        spent += used
-        samples += 1
-        e0 = (e0 + 37 * n_exp) % (E_local - n_exp + 1)
-    call_s = statistics.mean(est)
-    return {"value": round(T_EP / call_s, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{samples} samples of {n_exp} of {E_local} experts with all their routed tokens of T={T_EP}, "
-                      f"oracle (torch fp32 CPU + C router) extrapolated x{E_local // n_exp}; "
-                      f"{spent:.1f} s of CPU work",
-            "seconds_per_call_estimate": round(call_s, 2)}
+CPU_EXPERTS_PER_STEP = 4
 
 
-def _sample_block(cpu, inp, e0, n_exp, E_local):
-    """Oracle on experts [e0, e0+n_exp) of the shard (all their routed tokens): returns
-    (extrapolated seconds for the whole shard, seconds actually spent)."""
+def cpu_sample_steps(logits, bias, hs, hs_scale, E_local, n_steps, n_exp=CPU_EXPERTS_PER_STEP, seed=1000):
+    """The reference's algorithm (the oracle's restatement of run(), solution/triton/main.py:2430-2609) on the
+    host cores, one bounded sample per step: n_exp of the shard's E_local experts with every token routed to
+    them (their rows dequantised, then per expert: W13/W2 dequantisation, GEMM1, SwiGLU, GEMM2, weighted
+    accumulation).  Each step stands for the fraction n_exp / E_local of the layer, i.e. T * n_exp / E_local
+    tokens.  The routing of all T tokens (about 0.1 s per call, under 1 % of it) is computed once, outside the
+    steps.  Returns (per-step seconds, tokens per step, description)."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import fbmoe_workloads as W
     import oracle as O
-    t0 = time.perf_counter()
-    routing = O.route(cpu["routing_logits"], cpu["routing_bias"], cpu["routed_scaling_factor"])
-    t_route = time.perf_counter() - t0
-    t1 = time.perf_counter()
-    O.run(cpu["routing_logits"], cpu["routing_bias"], cpu["hidden_states"], cpu["hidden_states_scale"],
-          cpu["gemm1_weights"], cpu["gemm1_weights_scale"], cpu["gemm2_weights"], cpu["gemm2_weights_scale"],
-          int(inp["local_expert_offset"]) + e0, cpu["routed_scaling_factor"], routing=routing)
-    t_exp = time.perf_counter() - t1
-    return t_route + t_exp * (E_local / n_exp), t_route + t_exp
+    T = logits.shape[0]
+    routing = O.route(logits, bias, 2.5)
+    idx = routing[0]
+    w1, s1, w2, s2 = W.make_weights(n_exp, seed, "cpu")  # the sample's experts (same distributions)
+    times = []
+    for i in range(n_steps):
+        e0 = (i * 37 * n_exp) % (E_local - n_exp + 1)
+        rows = np.nonzero(((idx >= e0) & (idx < e0 + n_exp)).any(axis=1))[0]
+        t0 = time.perf_counter()
+        O.run(logits, bias, hs, hs_scale, w1, s1, w2, s2, e0, 2.5, tokens=rows, routing=routing)
+        times.append(time.perf_counter() - t0)
+    desc = (f"each step: {n_exp} of {E_local} experts with all their routed tokens of T={T} "
+            f"(= {T * n_exp / E_local:.0f} tokens of the layer's work), oracle restatement of the reference's "
+            f"run() (torch fp32 CPU + C router); routing of all T tokens once outside the steps")
+    return times, T * n_exp / E_local, desc
+
+
+def cpu_baseline_ep(inp, E_local, n_steps=4):
+    """cpu_baseline for the N=1 line: a few sample steps of the reference algorithm on the host cores."""
+    keys = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    logits, bias, hs, hs_scale = (inp[k].cpu() for k in keys)
+    times, tok, desc = cpu_sample_steps(logits, bias, hs, hs_scale, E_local, n_steps)
+    step_s = statistics.median(times)
+    return {"value": round(tok / step_s, 2), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n_steps} steps; " + desc, "seconds_per_step": round(step_s, 3),
+            "seconds_per_call_estimate": round(step_s * E_local / CPU_EXPERTS_PER_STEP, 1)}
 
 
 def run_reference(args, world, rank):
-    """The reference algorithm on the host cores (oracle restatement of run()), rank 0 only."""
+    """The reference algorithm on the host cores (oracle restatement of run()), rank 0 only; same metric, unit
+    and config as our arm.  Every step is a bounded sample of the workload (cpu_sample_steps); ms_per_step is the
+    measured wall time of a step and value the tokens it stands for per second."""
     if rank != 0:
         return None
     import fbmoe_workloads as W
     torch.set_num_threads(os.cpu_count() or 1)
     E_local = E_TOTAL // world
-    n_exp = 2
     logits, bias, hs, hs_scale = W.make_activations(T_EP, seed=0, config="standard", device="cpu")
-    cpu = {"routing_logits": logits, "routing_bias": bias, "hidden_states": hs, "hidden_states_scale": hs_scale,
-           "routed_scaling_factor": 2.5}
-    est = []
-    total = 0.0
-    for i in range(args.warmup + args.steps):
-        e0 = (i * 37 * n_exp) % (E_local - n_exp + 1)
-        w1, s1, w2, s2 = W.make_weights(n_exp, 1000 + e0, "cpu")
-        cpu.update(gemm1_weights=w1, gemm1_weights_scale=s1, gemm2_weights=w2, gemm2_weights_scale=s2)
-        full, used = _sample_block(cpu, {"local_expert_offset": 0}, e0, n_exp, E_local)
-        if i >= args.warmup:
-            est.append(full)
-            total += used
-    call_s = statistics.mean(est)
-    value = T_EP / call_s
+    times, tok, desc = cpu_sample_steps(logits, bias, hs, hs_scale, E_local, args.warmup + args.steps)
+    timed = times[args.warmup:]
+    total = sum(timed)
+    value = tok * len(timed) / total
     return {
-        "impl": "reference", "metric": "tokens/s per MoE layer call (DS-V3 FP8 MoE, T=8192, 256 experts, EP over N GPUs)",
+        "impl": "reference", "metric": METRIC,
         "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(call_s * 1e3, 1), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "fp32 (reference run(): fp32 dequantisation and matmul on CPU)", "data": "synthetic",
-        "config": {"workload": "config3_ep_T8192_E256", "T": T_EP, "E_total": E_TOTAL, "E_local": E_local,
-                   "parallelism": f"ep{world} (rank 0 shard on host cores)"},
+        "ms_per_step": round(1e3 * total / len(timed), 1), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32 (reference run(): fp32 dequantisation and matmul on CPU)",
+        "data": "synthetic (seeded N(0,1) activations/logits, N(0,0.02) weights, FP8 block-quantised)",
+        "config": workload_config(world),
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"each step: {n_exp} of {E_local} experts with all their routed tokens, "
-                                   f"extrapolated x{E_local // n_exp}; {total:.1f} s of CPU work in the timed steps"},
+                         "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -638,7 +638,6 @@ def main():
                          "NCCL reduce-scatter (nccl)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--case", choices=("ep", "decode", "prefill", "shard"), default="ep",
                     help="ep = the benchmark line (default); decode/prefill/shard = one small config for profiling "
                          "(shard = uniform routing over 32 local experts: one rank's work at N=8 when T=8192)")

@@ -66,9 +66,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Kernels of the forward are launched with programmatic stream serialization:
 // a kernel may start while its predecessor is still running.  pdl_wait() blocks
 // the calling thread until the predecessor grid has completed and its writes are
-// visible; pdl_trigger() lets the successor grid be scheduled.  Every kernel
-// triggers only after its own wait, so anything a successor reads before its
-// wait comes from grids that have already completed.
+// visible; pdl_trigger() lets the successor grid be scheduled.  The invariant the
+// kernels rely on: anything a kernel reads before its own pdl_wait() was written
+// by a grid at least two launches back in the stream (which has completed,
+// because the predecessor itself waited for it before it could finish).  Most
+// kernels trigger only after their wait; gemm2_rows_kernel triggers first (its
+// successor, the reduce or the expert-parallel flag release, waits before reading).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // After pdl_wait, before TMA (async proxy) reads of what the predecessor wrote.
@@ -142,6 +145,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > budget_ns) return false;
     }
+  }
+}
+
+// Wait for copies this CTA issued itself (TMA loads, MMA completion) before the
+// shared memory or tensor memory they target is reused or released.  Unlike
+// mbar_wait it ignores the CTA abort flag: after an abort the copies already in
+// flight still land within microseconds, and a CTA must not retire before they
+// do.  Bounded by `budget_ns`; returns false if the budget ran out.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t budget_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if ((it & 15u) == 0 && globaltimer_ns() - t0 > budget_ns) return false;
+  }
+}
+
+// At the end of a forward's last kernel: if the status word is non-zero, copy it
+// to the caller's host-visible sink (pinned host memory registered with
+// fbmoe_set_status_sink), so the host learns of a device-side error without a
+// synchronising read.  Racing CTAs may store different non-zero words; any of
+// them marks the call as failed.
+__device__ __forceinline__ void forward_status_to_sink(uint32_t* status, uint32_t* sink) {
+  if (sink == nullptr) return;
+  const uint32_t s = atomicOr(status, 0u);  // read at L2, after every earlier atomicOr
+  if (s != 0u) {
+    *reinterpret_cast<volatile uint32_t*>(sink) = s;
+    __threadfence_system();
   }
 }
 

@@ -7,6 +7,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace fbmoe {
 
 // Launch with programmatic stream serialization (see pdl_wait/pdl_trigger).
@@ -24,6 +26,43 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Cooperative launch (the whole grid is resident at once, or the launch fails),
+// optionally also with programmatic stream serialization.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                               bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Raises a kernel's dynamic shared-memory limit on the current device once per
+// device.  Safe from several host threads: the flags are atomic and the
+// attribute call is idempotent, so two first calls may both make it.
+constexpr int kMaxDevicesTracked = 64;
+using DeviceFlags = std::atomic<bool>[kMaxDevicesTracked];
+template <typename Kernel>
+inline cudaError_t set_max_dynamic_smem(Kernel kernel, int bytes, DeviceFlags& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < kMaxDevicesTracked;
+  if (tracked && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && tracked) done[dev].store(true, std::memory_order_release);
+  return e;
 }
 
 // Offsets (bytes) of the sub-buffers inside the caller-provided workspace.
@@ -98,10 +137,24 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
 // Decode (16-row blocks): GEMM1 + SwiGLU, GEMM2 x routing weight and the
 // per-token combine in one persistent kernel; writes out (bf16, or fp32 partial
 // sums with f32_out).
+// sink: host-visible status sink of the workspace (nullptr: none).
 cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
-                          cudaStream_t stream);
+                          uint32_t* sink, cudaStream_t stream);
+// 0: no decode launch yet; 1: cooperative with programmatic serialization;
+// 2: cooperative; 3: plain programmatic launch sized by the occupancy query.
+int decode_launch_mode();
+
+// Status sink registered for a workspace (fbmoe_set_status_sink), or nullptr.
+uint32_t* status_sink_for(const void* workspace);
+
+// Test hook (fbmoe_test_expire_grid_wait): while set, the decode kernel's grid
+// arrival waits for one arrival that never comes, with a budget of
+// kTestGridWaitNs, so every CTA's bounded wait expires and reports
+// kStatusTimeoutEpilogue without any fault.
+bool test_expire_grid_wait();
+constexpr uint64_t kTestGridWaitNs = 2000000ull;
 
 // GEMM1 + SwiGLU for blocks of 128 rows with the tokens as the MMA M operand.
 cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
@@ -116,7 +169,8 @@ cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm
 
 // out[t, :] = sum of the token's pair rows, fp32 accumulation; bf16 result, or
 // fp32 (f32_out) for partial sums that another stage combines across ranks.
-cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, cudaStream_t stream);
+cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, uint32_t* sink,
+                          cudaStream_t stream);
 
 // The whole forward on a caller-provided workspace (argument checks, TMA
 // descriptors, the five launches); the public entry points wrap it.

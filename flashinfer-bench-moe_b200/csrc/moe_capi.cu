@@ -11,6 +11,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "fbmoe.h"
@@ -111,13 +112,17 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes
 }
 
 static int num_sms_of_current_device() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[kMaxDevicesTracked];  // 0 = not looked up yet
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (dev < 64 && cache[dev]) return cache[dev];
+  const bool tracked = dev >= 0 && dev < kMaxDevicesTracked;
+  if (tracked) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int n = 148;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  if (dev < 64) cache[dev] = n;
+  if (tracked) cache[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -140,6 +145,29 @@ static void prof_record(int fwd, int point, cudaStream_t stream) {
 }
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Status sinks: workspace -> device-visible address of a pinned host word.  A
+// small table under a mutex; forward_core skips the lock while it is empty.
+constexpr int kMaxSinks = 64;
+struct SinkTable {
+  std::mutex mu;
+  std::atomic<int> n{0};
+  const void* ws[kMaxSinks] = {};
+  uint32_t* sink[kMaxSinks] = {};
+};
+static SinkTable g_sinks;
+
+uint32_t* status_sink_for(const void* workspace) {
+  if (g_sinks.n.load(std::memory_order_acquire) == 0) return nullptr;
+  std::lock_guard<std::mutex> lk(g_sinks.mu);
+  const int n = g_sinks.n.load(std::memory_order_relaxed);
+  for (int i = 0; i < n; ++i)
+    if (g_sinks.ws[i] == workspace) return g_sinks.sink[i];
+  return nullptr;
+}
+
+static std::atomic<int> g_test_expire{0};
+bool test_expire_grid_wait() { return g_test_expire.load(std::memory_order_relaxed) != 0; }
 
 }  // namespace fbmoe
 
@@ -205,6 +233,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   const int bn = force_rows ? force_rows : choose_block_rows(T, E_local);
   const int sms = num_sms_of_current_device();
+  uint32_t* sink = status_sink_for(workspace);
 
   CUtensorMap tm_w1, tm_w2, tm_inter, tm_w2raw, tm_aperm, tm_ascale;
   int rc = encode_2d(&tm_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm1_weights, kHidden, (uint64_t)E_local * kGemm1N,
@@ -260,7 +289,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
     // decode: GEMM1, GEMM2 and the combine run as one kernel (its time is the
     // "gemm1" stage of the profile; "gemm2" and "combine" stay empty)
     e = launch_decode(&tm_w1, &tm_w2, &tm_inter, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale,
-                      T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, stream);
+                      T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, sink, stream);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 3, stream);
     prof_record(fwd, 4, stream);
@@ -275,7 +304,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 4, stream);
     // with the scatter, the owners' combine (moe_ep.cu) replaces the local reduce
-    if (!scattering) e = launch_reduce(T, L, ws, out, f32_out, stream);
+    if (!scattering) e = launch_reduce(T, L, ws, out, f32_out, sink, stream);
   }
   prof_record(fwd, 5, stream);
   return from_cuda(e);
@@ -367,6 +396,52 @@ int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream_) {
   if (e != cudaSuccess) return from_cuda(e);
   return *status ? FBMOE_ERR_DEVICE_STATUS : FBMOE_OK;
 }
+
+int fbmoe_set_status_sink(const void* workspace, uint32_t* sink) {
+  if (!workspace) return FBMOE_ERR_NULL_POINTER;
+  uint32_t* dev_sink = nullptr;
+  if (sink) {
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, sink);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return FBMOE_ERR_INVALID_ARG;
+    }
+    if (attr.type != cudaMemoryTypeHost || attr.devicePointer == nullptr) return FBMOE_ERR_INVALID_ARG;
+    if (!aligned(sink, 4)) return FBMOE_ERR_MISALIGNED;
+    dev_sink = static_cast<uint32_t*>(attr.devicePointer);
+  }
+  std::lock_guard<std::mutex> lk(g_sinks.mu);
+  int n = g_sinks.n.load(std::memory_order_relaxed);
+  int at = -1;
+  for (int i = 0; i < n; ++i)
+    if (g_sinks.ws[i] == workspace) at = i;
+  if (!dev_sink) {  // unregister
+    if (at >= 0) {
+      g_sinks.ws[at] = g_sinks.ws[n - 1];
+      g_sinks.sink[at] = g_sinks.sink[n - 1];
+      g_sinks.n.store(n - 1, std::memory_order_release);
+    }
+    return FBMOE_OK;
+  }
+  if (at < 0) {
+    if (n == kMaxSinks) return FBMOE_ERR_INVALID_ARG;
+    at = n;
+    g_sinks.ws[at] = workspace;
+    g_sinks.sink[at] = dev_sink;
+    g_sinks.n.store(n + 1, std::memory_order_release);
+  } else {
+    g_sinks.sink[at] = dev_sink;
+  }
+  return FBMOE_OK;
+}
+
+int fbmoe_test_expire_grid_wait(int enable) {
+  g_test_expire.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return FBMOE_OK;
+}
+
+int fbmoe_decode_launch_mode(void) { return decode_launch_mode(); }
 
 const char* fbmoe_error_string(int code) {
   switch (code) {

@@ -151,9 +151,12 @@ struct DecodeArgs {
   __half* pair_out;
   void* out;
   uint32_t* status;
+  uint32_t* sink;          // host-visible copy of a non-zero status word (nullptr: none)
   size_t plane_elems;
   int T;
   int f32_out;
+  int grid_extra;          // arrivals the combine waits for beyond gridDim.x (0; 1 only under the test hook)
+  uint64_t grid_wait_ns;   // budget of the grid arrival wait
 };
 
 // Ring position: slot and phase parity of successive uses of a ring of n slots.
@@ -333,7 +336,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       // drain: every issued TMA load must have landed before the smem is reused
       for (int s = 0; s < S; ++s)
         if (last_parity[s] != 0xFFFFFFFFu)
-          if (!mbar_wait(&full[s], last_parity[s], sAbort, kWaitBudgetNs) && !*sAbort) fail(kStatusTimeoutDrain);
+          if (!mbar_wait_drain(&full[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -374,7 +377,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       if (any) {
         // all issued MMAs complete before TMEM and shared memory are reused
         tc_commit(drain);
-        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+        mbar_wait_drain(drain, 0, kWaitBudgetNs);
       }
     }
     __syncwarp();
@@ -585,7 +588,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       // every issued TMA load lands before the CTA exits
       for (int s = 0; s < n; ++s)
         if (last_parity[s] != 0xFFFFFFFFu)
-          if (!mbar_wait(&fullb[s], last_parity[s], sAbort, kWaitBudgetNs) && !*sAbort) fail(kStatusTimeoutDrain);
+          if (!mbar_wait_drain(&fullb[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -636,7 +639,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       }
       if (any) {
         tc_commit(drain);
-        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+        mbar_wait_drain(drain, 0, kWaitBudgetNs);
       }
     }
     __syncwarp();
@@ -780,8 +783,8 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volat
   if (first < tasks) prep(first);
   if (threadIdx.x == 0) {
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_gpu(a.grid_sync) < (int)gridDim.x) {
-      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+    while (ld_acquire_gpu(a.grid_sync) < (int)gridDim.x + a.grid_extra) {
+      if (globaltimer_ns() - t0 > a.grid_wait_ns) {
         *sAbort = 1;
         atomicOr(a.status, kStatusTimeoutEpilogue);
         break;
@@ -927,22 +930,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  // The decode kernel is the last of the call: a status bit set by any kernel of
+  // the call (this CTA's included, ordered by the barrier above) reaches the sink.
+  if (threadIdx.x == 0) forward_status_to_sink(a.status, a.sink);
 }
 
 }  // namespace
 
+// How the decode kernel was last launched (fbmoe_decode_launch_mode).
+static std::atomic<int> g_decode_mode{0};
+
+int decode_launch_mode() { return g_decode_mode.load(std::memory_order_relaxed); }
+
 cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
-                          cudaStream_t stream) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+                          uint32_t* sink, cudaStream_t stream) {
+  static DeviceFlags attr_set;
+  if (cudaError_t err = set_max_dynamic_smem(decode_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
   DecodeArgs a;
   a.tm_w1 = *tm_w1;
   a.tm_w2 = *tm_w2;
@@ -965,10 +970,45 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.pair_out = reinterpret_cast<__half*>(ws + L.pair_out);
   a.out = out;
   a.status = reinterpret_cast<uint32_t*>(ws + L.status);
+  a.sink = sink;
   a.plane_elems = (size_t)L.pcap * kHidden;
   a.T = T;
   a.f32_out = f32_out ? 1 : 0;
+  const bool expire = test_expire_grid_wait();
+  a.grid_extra = expire ? 1 : 0;
+  a.grid_wait_ns = expire ? kTestGridWaitNs : kWaitBudgetNs;
+  // Every CTA waits at the grid arrival for all the others, so the whole grid
+  // must be resident at once: one CTA per SM (the occupancy query confirms that
+  // one fits), launched cooperatively so that the launch itself guarantees it
+  // even when other work holds SMs.  The first launch on a device tries the
+  // cooperative launch with programmatic serialization, then without it; if the
+  // driver refuses both, the grid falls back to a plain launch sized by the
+  // occupancy query (the arrival wait is bounded either way).
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel, kThreads, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  if (occ < 1) return cudaErrorInvalidConfiguration;
   const int grid = num_sms > 0 ? num_sms : 1;
+  const int mode = g_decode_mode.load(std::memory_order_relaxed);
+  if (mode == 0 || mode == 1) {
+    e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, true, a);
+    if (e == cudaSuccess) {
+      g_decode_mode.store(1, std::memory_order_relaxed);
+      return e;
+    }
+    if (mode == 1) return e;
+    (void)cudaGetLastError();  // a refused launch configuration is not a sticky error
+  }
+  if (mode == 0 || mode == 2) {
+    e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, false, a);
+    if (e == cudaSuccess) {
+      g_decode_mode.store(2, std::memory_order_relaxed);
+      return e;
+    }
+    if (mode == 2) return e;
+    (void)cudaGetLastError();
+  }
+  g_decode_mode.store(3, std::memory_order_relaxed);
   return launch_pdl(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, a);
 }
 

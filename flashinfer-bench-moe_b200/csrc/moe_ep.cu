@@ -95,7 +95,7 @@ __global__ void ep_signal_kernel(const FlagTable ft, int world, uint32_t epoch) 
 __global__ void __launch_bounds__(kCombineThreads) ep_combine_kernel(const uint32_t* flags, int world, uint32_t epoch,
                                                                    const __half* pairs, int rows,
                                                                    __nv_bfloat16* __restrict__ out,
-                                                                   uint32_t* status) {
+                                                                   uint32_t* status, uint32_t* sink) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     int good = 1;
@@ -111,6 +111,8 @@ __global__ void __launch_bounds__(kCombineThreads) ep_combine_kernel(const uint3
     }
     if (!good) atomicOr(status, kStatusTimeoutPeer);
     ok = good;
+    // the last kernel of the call on this rank (its own send kernels have completed)
+    if (blockIdx.x == 0 || !good) forward_status_to_sink(status, sink);
   }
   __syncthreads();
   if (!ok) return;
@@ -287,7 +289,7 @@ int fbmoe_forward_ep_recv(const void* my_recv, int T, int rank, int world, uint3
   if (grid > (long)sms * 8) grid = (long)sms * 8;
   ep_combine_kernel<<<(unsigned)grid, kCombineThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint32_t*>(base), world, epoch, pairs, rows,
-      static_cast<__nv_bfloat16*>(out_rows_bf16), static_cast<uint32_t*>(workspace));
+      static_cast<__nv_bfloat16*>(out_rows_bf16), static_cast<uint32_t*>(workspace), status_sink_for(workspace));
   return from_cuda_ep(cudaGetLastError());
 }
 

@@ -1,9 +1,9 @@
 // moe_gemm1_rows.cu -- GEMM1 + SwiGLU for large token blocks (prefill), with
 // the tokens as the MMA's M operand (tcgen05 kind::f8f6f4, TMEM, TMA), sm_100a.
 //
-// Same result as moe_gemm1.cu (reference gemm1_kernel + act_quant_kernel,
-// solution/triton/main.py:41-223, 1426-1602): per permuted row r (token t) of
-// expert e,
+// Counterpart of the reference's gemm1_kernel + act_quant_kernel (solution/
+// triton/main.py:41-223, 1426-1602), and the same arithmetic as the GEMM1 phase
+// of moe_decode.cu: per permuted row r (token t) of expert e,
 //     G1[r, n] = sum_k A[t, k] * a_scale[k/128, t] * W1[e, n, k] * s1[e, n/128, k/128]
 //     inter[r, j] = silu(G1[r, 2048 + j]) * G1[r, j]      (f16, clamped to +-65504)
 //
@@ -171,16 +171,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every issued load lands before the CTA exits
       for (int s = 0; s < kStages; ++s)
         if ((issued_mask >> s) & 1u)
-          if (!mbar_wait(&full[s], (parity_mask >> s) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+          if (!mbar_wait_drain(&full[s], (parity_mask >> s) & 1u, kWaitBudgetNs))
             fail(kStatusTimeoutDrain);
       for (int k = 1; k <= kScaleSlots && k <= x; ++k) {
         const int y = x - k;  // the last K-blocks issued, one per slot
-        if (!mbar_wait(&sfull[y & (kScaleSlots - 1)], (uint32_t)(y >> 3) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+        if (!mbar_wait_drain(&sfull[y & (kScaleSlots - 1)], (uint32_t)(y >> 3) & 1u, kWaitBudgetNs))
           fail(kStatusTimeoutDrain);
       }
       for (int k = 1; k <= 2 && k <= ui; ++k) {
         const int v = ui - k;
-        if (!mbar_wait(&wfull[v & 1], (uint32_t)(v >> 1) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+        if (!mbar_wait_drain(&wfull[v & 1], (uint32_t)(v >> 1) & 1u, kWaitBudgetNs))
           fail(kStatusTimeoutDrain);
       }
     }
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (any) {
         tc_commit(drain);
-        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+        mbar_wait_drain(drain, 0, kWaitBudgetNs);
       }
     }
     __syncwarp();
@@ -320,14 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
                               const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
                               cudaStream_t stream) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(gemm1_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+  static DeviceFlags attr_set;
+  if (cudaError_t err = set_max_dynamic_smem(gemm1_rows_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
   const long max_units = (long)L.max_blocks * kTiles;
   int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (grid < 1) grid = 1;

@@ -1,8 +1,9 @@
 // moe_gemm2_rows.cu -- GEMM2 x routing weight for large token blocks (prefill),
 // tokens as the MMA's M operand (tcgen05 kind::f16, TMEM, TMA), sm_100a.
 //
-// Same result as moe_gemm2.cu (reference gemm2_kernel, solution/triton/main.py:
-// 433-600): pair_out[r, h] = w[r] * sum_j inter[r, j] * W2[e, h, j] * s2[e, h/128, j/128].
+// Counterpart of the reference's gemm2_kernel (solution/triton/main.py:433-600),
+// and the same arithmetic as the GEMM2 phase of moe_decode.cu:
+//     pair_out[r, h] = w[r] * sum_j inter[r, j] * W2[e, h, j] * s2[e, h/128, j/128].
 //
 // Orientation.  A = 128 intermediate rows (f16, TMA, 128-byte swizzle);
 // B = 256 W2 rows = two 128-row scale blocks of the hidden dimension, converted
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int s = 0; s < n; ++s)
         if ((issued_mask >> s) & 1u)
-          if (!mbar_wait(&fullb[s], (parity_mask >> s) & 1u, sAbort, kWaitBudgetNs) && !*sAbort)
+          if (!mbar_wait_drain(&fullb[s], (parity_mask >> s) & 1u, kWaitBudgetNs))
             fail(kStatusTimeoutDrain);
     }
     __syncwarp();
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (any) {
         tc_commit(drain);
-        mbar_wait(drain, 0, sAbort, kWaitBudgetNs);
+        mbar_wait_drain(drain, 0, kWaitBudgetNs);
       }
     }
     __syncwarp();
@@ -385,14 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
                               const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream,
                               const PeerScatter* scatter) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(gemm2_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+  static DeviceFlags attr_set;
+  if (cudaError_t err = set_max_dynamic_smem(gemm2_rows_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
   PeerScatter ps{};
   if (scatter != nullptr) ps = *scatter;
   const long max_units = (long)L.max_blocks * kNTiles;

@@ -18,9 +18,16 @@
 // different host threads without ordering) race on it.
 //
 // Set-up: the first call on each device looks up the array's device address
-// with cudaGetSymbolAddress while that device is current.  Make that first
-// call before any stream capture begins.  No call allocates or frees device
-// memory.
+// with cudaGetSymbolAddress while that device is current.  With lazy module
+// loading (the CUDA default), that lookup is also what makes the driver load
+// this library's device code on the device, and with it commit the 12 MiB
+// array.  So make the first call at set-up time, before any stream capture
+// begins and before any memory budget on the hot path applies; after it, no
+// call allocates or frees device memory.
+//
+// Errors: device-side status bits (a bounded wait that expired, an f16 value
+// clamped) land in the array's status word; fbmoe_noalloc_read_status reads the
+// word of the last call on the current device.
 #include <mutex>
 
 #include "fbmoe.h"
@@ -61,6 +68,17 @@ int scratch_for_current_device(void** out) {
 
 }  // namespace
 }  // namespace fbmoe
+
+extern "C" int fbmoe_noalloc_read_status(uint32_t* status, void* stream) {
+  using namespace fbmoe;
+  if (!status) return FBMOE_ERR_NULL_POINTER;
+  *status = 0;
+  void* scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc != FBMOE_OK) return rc;
+  // the status word sits at offset 0 of the forward's layout (make_layout)
+  return fbmoe_read_status(scratch, status, stream);
+}
 
 extern "C" int fbmoe_forward_noalloc(const float* routing_logits, const void* routing_bias, const void* hidden_states,
                                      const float* hidden_states_scale, const void* gemm1_weights,

@@ -403,15 +403,8 @@ constexpr int kFusedSmem = kFusedT * (3 * kExperts + kTopK) * 4;
 cudaError_t launch_route_permute_small(const float* logits, const void* bias_bf16, int T, float scale, int E_local,
                                        int local_offset, int bn, const Layout& L, uint8_t* ws, cudaStream_t stream) {
   if (T < 1 || T > kFusedT) return cudaErrorInvalidValue;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(route_permute_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kFusedSmem);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+  static DeviceFlags attr_set;
+  if (cudaError_t err = set_max_dynamic_smem(route_permute_small_kernel, kFusedSmem, attr_set); err != cudaSuccess) return err;
   return launch_pdl(route_permute_small_kernel, dim3(1), dim3(kSmallThreads), kFusedSmem, stream, logits,
       reinterpret_cast<const __nv_bfloat16*>(bias_bf16), scale, reinterpret_cast<int32_t*>(ws + L.topk_idx),
       reinterpret_cast<float*>(ws + L.topk_w), T, E_local, local_offset, bn,
@@ -425,15 +418,9 @@ cudaError_t launch_route_permute_small(const float* logits, const void* bias_bf1
 
 cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, int E_local, int local_offset,
                            int bn, int num_sms, const Layout& L, uint8_t* ws, cudaStream_t stream) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
   const int smem = (int)sizeof(PermuteSmem);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+  static DeviceFlags attr_set;
+  if (cudaError_t err = set_max_dynamic_smem(permute_kernel, smem, attr_set); err != cudaSuccess) return err;
   if (T > 0 && T <= kSmallT)
     return launch_pdl(permute_small_kernel, dim3(1), dim3(kSmallThreads), 0, stream, topk_idx, topk_w, T, E_local,
         local_offset, bn, reinterpret_cast<int32_t*>(ws + L.expert_cnt), reinterpret_cast<int32_t*>(ws + L.expert_poff),

@@ -19,8 +19,11 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __
                                                                 const int32_t* __restrict__ token_rows,
                                                                 void* __restrict__ out_,
                                                                 const int32_t* __restrict__ splits,
-                                                                size_t plane_elems) {
+                                                                size_t plane_elems, uint32_t* status,
+                                                                uint32_t* sink) {
   pdl_wait();
+  // the last kernel of the call: every earlier kernel's status bits are visible now
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) forward_status_to_sink(status, sink);
   const int t = blockIdx.y;
   const int col = (blockIdx.x * kReduceThreads + threadIdx.x) * 8;
   float acc[8];
@@ -63,16 +66,20 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __
 
 }  // namespace
 
-cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, cudaStream_t stream) {
+cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f32_out, uint32_t* sink,
+                          cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   dim3 grid(kReduceChunks, T);
   const __half* pairs = reinterpret_cast<const __half*>(ws + L.pair_out);
   const int32_t* rows = reinterpret_cast<const int32_t*>(ws + L.token_rows);
   const int32_t* splits = reinterpret_cast<const int32_t*>(ws + L.splits);
   const size_t plane = (size_t)L.pcap * kHidden;
+  uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
   if (f32_out)
-    return launch_pdl(reduce_kernel<true>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane);
-  return launch_pdl(reduce_kernel<false>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane);
+    return launch_pdl(reduce_kernel<true>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane,
+                      status, sink);
+  return launch_pdl(reduce_kernel<false>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane,
+                    status, sink);
 }
 
 }  // namespace fbmoe

@@ -1,4 +1,4 @@
-"""Expert parallelism across the GPUs of one node (SURVEY §8e).
+"""Expert parallelism across the GPUs of one node.
 
 The 256 experts shard by contiguous ranges: rank r of N owns experts
 [r*256/N, (r+1)*256/N) and passes that range to the operator through

@@ -64,6 +64,14 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_block_rows.restype = i32
         lib.fbmoe_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32), vp]
         lib.fbmoe_read_status.restype = i32
+        lib.fbmoe_noalloc_read_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), vp]
+        lib.fbmoe_noalloc_read_status.restype = i32
+        lib.fbmoe_set_status_sink.argtypes = [vp, vp]
+        lib.fbmoe_set_status_sink.restype = i32
+        lib.fbmoe_decode_launch_mode.argtypes = []
+        lib.fbmoe_decode_launch_mode.restype = i32
+        lib.fbmoe_test_expire_grid_wait.argtypes = [i32]
+        lib.fbmoe_test_expire_grid_wait.restype = i32
         lib.fbmoe_error_string.argtypes = [i32]
         lib.fbmoe_error_string.restype = ctypes.c_char_p
         lib.fbmoe_version.argtypes = []
@@ -125,20 +133,93 @@ def block_rows(T: int, E_local: int) -> int:
 
 
 # One workspace per (device, stream): calls on one stream are ordered, so reuse is safe.
+# Each cached workspace has a status sink: one pinned host word into which the
+# last kernel of every forward stores the call's device status word when it is
+# non-zero (fbmoe_set_status_sink), so errors surface without a host sync.
 _workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+_sinks: Dict[Tuple[int, int], torch.Tensor] = {}
+_sink_words: Dict[Tuple[int, int], ctypes.c_uint32] = {}  # the same pinned words, read without torch overhead
 _ws_lock = threading.Lock()
+
+STATUS_BITS = (
+    (0x1, "a producer's bounded wait expired"),
+    (0x2, "the MMA issuer's bounded wait expired"),
+    (0x4, "an epilogue or grid-arrival wait expired"),
+    (0x8, "a converter's bounded wait expired"),
+    (0x10, "the GEMM block list overflowed"),
+    (0x20, "draining in-flight copies timed out"),
+    (0x40, "an f16 intermediate or pair value was clamped to +-65504"),
+    (0x80, "a peer rank's pair rows did not arrive in time"),
+    (0x100, "a pair row's (token, slot) was not found"),
+)
+
+
+def describe_status(word: int) -> str:
+    parts = [msg for bit, msg in STATUS_BITS if word & bit]
+    return "; ".join(parts) if parts else "no error"
+
+
+class DeviceStatusError(RuntimeError):
+    """A kernel of a forward reported a device-side error (its status word was non-zero)."""
+
+    def __init__(self, word: int, where: str):
+        self.word = int(word)
+        super().__init__(f"fbmoe device status {self.word:#x} ({describe_status(self.word)}) {where}")
+
+
+def _workspace_key(device: torch.device, stream_handle: int) -> Tuple[int, int]:
+    return (device.index if device.index is not None else torch.cuda.current_device(), int(stream_handle))
 
 
 def get_workspace(nbytes: int, device: torch.device, stream_handle: int) -> torch.Tensor:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), int(stream_handle))
+    key = _workspace_key(device, stream_handle)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
+            lib = load_library()
+            if ws is not None:
+                _check(lib.fbmoe_set_status_sink(ws.data_ptr(), None))
             # grow geometrically so that a ragged sequence of T does not reallocate every call
             size = max(nbytes, int(ws.numel() * 1.5) if ws is not None else 0)
             ws = torch.empty(size, dtype=torch.uint8, device=device)
             _workspaces[key] = ws
+            sink = _sinks.get(key)
+            if sink is None:
+                sink = torch.zeros(1, dtype=torch.int32).pin_memory()
+                _sinks[key] = sink
+                _sink_words[key] = ctypes.c_uint32.from_address(sink.data_ptr())
+            _check(lib.fbmoe_set_status_sink(ws.data_ptr(), sink.data_ptr()))
         return ws
+
+
+def _take_sink(key) -> int:
+    """The sink's word for a cached workspace (cleared once read); 0 when clean."""
+    w = _sink_words.get(key)
+    if w is None:
+        return 0
+    word = int(w.value)
+    if word:
+        w.value = 0
+    return word
+
+
+def check_status(device: torch.device = None, synchronize: bool = True) -> None:
+    """Raise DeviceStatusError if any forward on a cached workspace of `device` (all devices if None) reported a
+    device-side error.  With ``synchronize`` the device is synchronised first, so every call issued so far is
+    covered; without it only the calls that have already finished are."""
+    if synchronize:
+        torch.cuda.synchronize(device)
+    for key in list(_sinks):
+        if device is not None and key[0] != torch.device(device).index:
+            continue
+        word = _take_sink(key)
+        if word:
+            raise DeviceStatusError(word, "reported by a forward on this device")
+
+
+def sync_status_default() -> bool:
+    """FBMOE_SYNC_STATUS=1 makes every forward synchronise and check its own status."""
+    return os.environ.get("FBMOE_SYNC_STATUS", "0") not in ("", "0")
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -195,11 +276,18 @@ def check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scal
 def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
             gemm2_weights, gemm2_weights_scale, local_expert_offset, routed_scaling_factor,
             out: torch.Tensor = None, workspace: torch.Tensor = None, check: bool = True,
-            partial_f32: bool = False) -> torch.Tensor:
+            partial_f32: bool = False, sync_status: bool = None) -> torch.Tensor:
     """Run the fused MoE on the current stream; returns bf16 [T, 7168] (a fresh tensor unless `out` is given).
 
     With ``partial_f32`` the un-rounded fp32 sum over the local experts is returned
-    instead (the expert-parallel partial)."""
+    instead (the expert-parallel partial).
+
+    Device-side errors (a bounded wait that expired, an f16 value clamped) raise
+    DeviceStatusError, a RuntimeError.  By default the check is asynchronous: the
+    call's last kernel stores a non-zero status word into the workspace's pinned
+    sink, and the next call on the same workspace (or check_status()) raises.
+    ``sync_status=True`` (or FBMOE_SYNC_STATUS=1) synchronises the stream after
+    the launch and raises for this call itself."""
     lib = load_library()
     if check:
         T, E = check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
@@ -215,14 +303,26 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         return out
     stream = torch.cuda.current_stream(dev).cuda_stream
     need = int(lib.fbmoe_workspace_size(T, E))
+    key = None
     if workspace is None:
         workspace = get_workspace(need, dev, stream)
+        key = _workspace_key(dev, stream)
+        word = _take_sink(key)
+        if word:
+            raise DeviceStatusError(word, "reported by an earlier forward on this stream's workspace")
     fn = lib.fbmoe_forward_partial_f32 if partial_f32 else lib.fbmoe_forward
     _check(fn(
         routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
         gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(), gemm2_weights.data_ptr(),
         gemm2_weights_scale.data_ptr(), int(T), int(E), int(local_expert_offset), float(routed_scaling_factor),
         out.data_ptr(), workspace.data_ptr(), int(workspace.numel()), stream))
+    if sync_status is None:
+        sync_status = sync_status_default()
+    if sync_status:
+        torch.cuda.current_stream(dev).synchronize()
+        word = _take_sink(key) if key is not None else read_status(workspace)
+        if word:
+            raise DeviceStatusError(word, "reported by this forward")
     return out
 
 
@@ -270,6 +370,23 @@ def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, routed_scali
     _check(lib.fbmoe_route(routing_logits.data_ptr(), routing_bias.data_ptr(), int(T), float(routed_scaling_factor),
                            idx.data_ptr(), w.data_ptr(), stream))
     return idx, w
+
+
+def decode_launch_mode() -> int:
+    """How the decode kernel was last launched (0 none yet, 1 cooperative + PDL, 2 cooperative, 3 plain)."""
+    return int(load_library().fbmoe_decode_launch_mode())
+
+
+def noalloc_read_status(stream_handle: int = None) -> int:
+    """Status word of the last fbmoe_forward_noalloc call on the current device (synchronises the stream)."""
+    lib = load_library()
+    st = ctypes.c_uint32(0)
+    if stream_handle is None:
+        stream_handle = torch.cuda.current_stream().cuda_stream
+    rc = lib.fbmoe_noalloc_read_status(ctypes.byref(st), stream_handle)
+    if rc not in (0, -6):
+        _check(rc)
+    return int(st.value)
 
 
 def read_status(workspace: torch.Tensor) -> int:

@@ -93,13 +93,25 @@ FBMOE_API int fbmoe_forward_partial_f32(const float* routing_logits, const void*
  * library's device code is loaded, until the process exits.  Every call shares
  * it: calls that overlap on the GPU (e.g. on two streams) race.  The first call
  * on a device looks up the array's address (cudaGetSymbolAddress) with that
- * device current; make it before any stream capture.  No call allocates or
- * frees device memory. */
+ * device current; with lazy module loading (the CUDA default) that lookup also
+ * makes the driver load the library's device code there and commit the 12 MiB
+ * array.  Make that first call at set-up, before any stream capture and before
+ * a hot-path memory budget applies; after it no call allocates or frees device
+ * memory.  Device-side errors: fbmoe_noalloc_read_status. */
 FBMOE_API int fbmoe_forward_noalloc(const float* routing_logits, const void* routing_bias,
                                     const void* hidden_states, const float* hidden_states_scale,
                                     const void* gemm1_weights, const float* gemm1_weights_scale,
                                     const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                                     int local_expert_offset, float routed_scaling_factor, void* out, void* stream);
+
+/* Device status word of the last fbmoe_forward_noalloc call on the current
+ * device (no counterpart in the reference; synchronises `stream`).  The array
+ * that holds the no-alloc workspace is private to the library, so this is the
+ * only way its callers can see a device-side error.  Returns
+ * FBMOE_ERR_DEVICE_STATUS when the word is non-zero (bits as for
+ * fbmoe_read_status).  Like fbmoe_forward_noalloc, the first call on a device
+ * looks up the array's address. */
+FBMOE_API int fbmoe_noalloc_read_status(uint32_t* status, void* stream);
 
 /* DeepSeek-V3 no-aux routing only (reference main.py:2522-2553 / fusedGatingKernel
  * main.py:851-1038).  topk_idx int32 [T, 8] global expert ids in canonical order
@@ -131,6 +143,29 @@ FBMOE_API int fbmoe_block_rows(int T, int E_local);
  * flags of an expert-parallel combine), the block list overflowed (bit 4), an f16
  * value was clamped (bit 6) or a pair row's slot was not found (bit 8). */
 FBMOE_API int fbmoe_read_status(const void* workspace, uint32_t* status, void* stream);
+
+/* Registers pinned host memory `sink` (one uint32, from cudaHostAlloc /
+ * cudaMallocHost, device-accessible) as the status sink of `workspace`; NULL
+ * unregisters.  The last kernel of every later forward on that workspace
+ * (fbmoe_forward, fbmoe_forward_partial_f32, the expert-parallel receive) stores
+ * the call's status word into the sink when it is non-zero, so a host can learn
+ * of a device-side error (the bits of fbmoe_read_status) by reading the sink,
+ * without synchronising.  The sink is sticky: the caller clears it.  At most 64
+ * workspaces have sinks.  No reference counterpart: the reference ignores
+ * launch and device status (main.py:2062-2070). */
+FBMOE_API int fbmoe_set_status_sink(const void* workspace, uint32_t* sink);
+
+/* How the decode kernel (T <= 64) was last launched: 0 not yet, 1 cooperative
+ * with programmatic serialization, 2 cooperative, 3 plain (grid sized by an
+ * occupancy query).  Its CTAs wait for one another, so the cooperative launch
+ * is what guarantees they are all resident. */
+FBMOE_API int fbmoe_decode_launch_mode(void);
+
+/* Test hook: while `enable` is non-zero the decode kernel's grid-arrival wait
+ * waits for one arrival that never comes, with a 2 ms budget, so every CTA's
+ * bounded wait expires, sets status bit 2 and returns without writing its part
+ * of the output.  Lets tests exercise the error path without any device fault. */
+FBMOE_API int fbmoe_test_expire_grid_wait(int enable);
 
 /* Stage timing for measurement: after fbmoe_profile_begin(n), the next n
  * forwards record CUDA events on their stream between the stages (route,

@@ -37,17 +37,34 @@ def _noalloc(lib, inp, out):
 
 
 def test_noalloc_matches_forward_twice(fbmoe_lib, workloads, oracle_mod):
+    """Calls in a row of different sizes (down, then back up) and a call whose tokens route to no
+    local expert (offset 224, logits pushed away from experts 224..255: the output must be all
+    zeros).  Each must match the workspace-taking entry point, and the array's status word must
+    read clean after each."""
     lib = _bind(fbmoe_lib.load_library())
     weights = workloads.make_weights(32, 606, "cuda")
-    for call, (T, config) in enumerate([(16, "group"), (5, "standard")]):
-        inp = workloads.make_inputs(T, seed=40 + call, config=config, device="cuda", weights=weights)
+    calls = [(16, "group", 0), (5, "standard", 0), (16, "standard", 0), (7, "away", 224)]
+    for call, (T, config, offset) in enumerate(calls):
+        inp = workloads.make_inputs(T, seed=40 + call, config=config, device="cuda", local_expert_offset=offset,
+                                    weights=weights)
         ref = fbmoe_lib.forward(*[inp[k] for k in ARGS], inp["local_expert_offset"], inp["routed_scaling_factor"])
         out = torch.full((T, 7168), float("nan"), dtype=torch.bfloat16, device="cuda")
         rc = _noalloc(lib, inp, out)
         assert rc == 0, lib.fbmoe_error_string(rc)
         torch.cuda.synchronize()
+        assert fbmoe_lib.noalloc_read_status() == 0, call
         st = oracle_mod.error_stats(out.cpu(), ref.cpu(), ATOL, RTOL)
         assert st["nonfinite"] == 0 and st["frac_pass"] == 1.0, (call, st)
+        if config == "away":
+            idx, _ = oracle_mod.route(inp["routing_logits"].cpu(), inp["routing_bias"].cpu(), 2.5)
+            if not ((idx >= offset) & (idx < offset + 32)).any():
+                assert out.abs().max().item() == 0.0
+
+
+def test_noalloc_zero_tokens_is_a_no_op(fbmoe_lib):
+    lib = _bind(fbmoe_lib.load_library())
+    nul = None
+    assert lib.fbmoe_forward_noalloc(*([nul] * 8), 0, 32, 0, 2.5, nul, nul) == 0
 
 
 def test_noalloc_rejects_sizes_beyond_its_limit(fbmoe_lib, workloads):
