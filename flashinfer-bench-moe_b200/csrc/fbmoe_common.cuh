@@ -41,7 +41,50 @@ enum StatusBits : uint32_t {
   kStatusSaturated = 1u << 6,  // an f16 intermediate/pair value was clamped to +-65504
   kStatusTimeoutPeer = 1u << 7,  // expert parallelism: a peer's pair rows did not arrive in time
   kStatusBadSlot = 1u << 8,      // expert parallelism: a pair row's (token, slot) was not found
+  kStatusDebugIndex = 1u << 9,   // debug-check build: an index read from the workspace was out of range
 };
+
+// ---------------------------------------------------------- debug checks ----
+// Debug-check build (-DFBMOE_DEBUG_CHECKS, libfbmoe_debug.so): every index a
+// kernel reads back from the workspace -- the token of a permuted row, the
+// permuted row of a (token, slot), a GEMM block's expert and row range -- is
+// range-checked before it addresses memory.  A bad value sets kStatusDebugIndex
+// and is replaced by a harmless one (token 0, no row, an empty block), so the
+// access it would have made is skipped or stays in bounds and the pipelines keep
+// their protocol.  The checks never trap.  In the normal build they compile to
+// nothing.  This is the stand-in for a memory checker on hardware where none runs.
+#ifdef FBMOE_DEBUG_CHECKS
+constexpr bool kDebugChecks = true;
+#else
+constexpr bool kDebugChecks = false;
+#endif
+
+// A token index in [0, n): otherwise 0.
+__device__ __forceinline__ int dbg_token(int v, int n, uint32_t* status) {
+  if (kDebugChecks && (unsigned)v >= (unsigned)n) {
+    atomicOr(status, kStatusDebugIndex);
+    return 0;
+  }
+  return v;
+}
+// A row index in [0, n) or -1 (none): otherwise -1.
+__device__ __forceinline__ int dbg_row(int v, int n, uint32_t* status) {
+  if (kDebugChecks && v != -1 && (unsigned)v >= (unsigned)n) {
+    atomicOr(status, kStatusDebugIndex);
+    return -1;
+  }
+  return v;
+}
+// A GEMM block (expert, first row, rows): expert in [0, e_local), rows in
+// [1, max_rows], all inside [0, pcap): otherwise an empty block of expert 0.
+__device__ __forceinline__ int4 dbg_block(int4 b, int max_rows, int e_local, int pcap, uint32_t* status) {
+  if (kDebugChecks && ((unsigned)b.x >= (unsigned)e_local || b.y < 0 || b.z < 1 || b.z > max_rows ||
+                       b.y + b.z > pcap)) {
+    atomicOr(status, kStatusDebugIndex);
+    return make_int4(0, 0, 0, 0);
+  }
+  return b;
+}
 
 constexpr float kF16Max = 65504.0f;
 

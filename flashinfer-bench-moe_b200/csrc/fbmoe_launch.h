@@ -88,6 +88,7 @@ struct Layout {
   size_t grid_sync;    // int32[1]: CTAs of the decode kernel done with GEMM2 (zeroed by permute)
   size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
   size_t total;        // bytes
+  int tokens;          // T the layout was made for
   int pcap;            // row capacity (multiple of 128)
   int e_local;         // local experts the layout was made for
   int pair_planes;     // planes of pair_out (GEMM2 K splits write separate planes)

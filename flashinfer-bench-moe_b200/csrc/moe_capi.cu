@@ -37,6 +37,7 @@ int choose_block_rows(int T, int E_local) {
 Layout make_layout(int T, int E_local, bool allow_split, int force_rows) {
   Layout L;
   const size_t tt = (size_t)(T > 0 ? T : 0);
+  L.tokens = (int)tt;
   const int el = E_local > 0 ? E_local : 0;
   long pcap = (long)tt * kTopK + (long)kRowAlign * el;
   pcap = (long)align_up((size_t)pcap, 128);

@@ -154,6 +154,8 @@ struct DecodeArgs {
   uint32_t* sink;          // host-visible copy of a non-zero status word (nullptr: none)
   size_t plane_elems;
   int T;
+  int pcap;                // row capacity of the workspace (bounds of the debug checks)
+  int e_local;
   int f32_out;
   int grid_extra;          // arrivals the combine waits for beyond gridDim.x (0; 1 only under the test hook)
   uint64_t grid_wait_ns;   // budget of the grid arrival wait
@@ -275,7 +277,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       const Seg sg = seg_at(P, x, x_end);
       x += sg.kb1 - sg.kb0;
       const int u = sg.u;
-      const int4 blk = a.blocks[u / kG1Slices];
+      const int4 blk = dbg_block(a.blocks[u / kG1Slices], BN, a.e_local, a.pcap, a.status);
       const int g = u % kG1Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
       // token row pointers for the rows this lane copies: rows (lane>>3) + 4j
@@ -284,7 +286,9 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 #pragma unroll
       for (int j = 0; j < kRowsPerLane; ++j) {
         const int row = (lane >> 3) + 4 * j;
-        src[j] = (row < nrows) ? a.hidden + (size_t)a.row_token[r0 + row] * kHidden + (lane & 7) * 16 : a.hidden;
+        src[j] = (row < nrows) ? a.hidden + (size_t)dbg_token(a.row_token[r0 + row], a.T, a.status) * kHidden +
+                                     (lane & 7) * 16
+                               : a.hidden;
       }
       const int wrow1 = e * kGemm1N + 64 * g;
       const int wrow2 = wrow1 + kInter;
@@ -396,10 +400,10 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       x += sg.kb1 - sg.kb0;
       const int u = sg.u, nk = sg.kb1 - sg.kb0;
       const int nseg = P.nseg(u);
-      const int4 blk = a.blocks[u / kG1Slices];
+      const int4 blk = dbg_block(a.blocks[u / kG1Slices], BN, a.e_local, a.pcap, a.status);
       const int g = u % kG1Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
-      if (etid < BN) sTok[etid] = (etid < nrows) ? a.row_token[r0 + etid] : -1;
+      if (etid < BN) sTok[etid] = (etid < nrows) ? dbg_token(a.row_token[r0 + etid], a.T, a.status) : -1;
       if (etid < 2 * kHBlocks) {
         const int h = etid / kHBlocks, kb = etid % kHBlocks;
         const int nbk = h * (kInter / kBlk) + g / 2;
@@ -547,7 +551,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         x += sg.kb1 - sg.kb0;
         const int u = sg.u;
         const int b = u / kG2Slices;
-        const int4 blk = a.blocks[b];
+        const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
         const int h = u % kG2Slices;
         const int e = blk.x, r0 = blk.y;
         if (!w2_side && b != ready_blk) {
@@ -665,7 +669,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         continue;
       }
       const int u = sg.u;
-      const int4 blk = a.blocks[u / kG2Slices];
+      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
       const int h = u % kG2Slices;
       const float* sc = a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
       const int kexp = w2_block_exponent(sc);
@@ -723,7 +727,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       x += sg.kb1 - sg.kb0;
       const int u = sg.u;
       const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
-      const int4 blk = a.blocks[u / kG2Slices];
+      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
       const int h = u % kG2Slices;
       const int r0 = blk.y, nrows = blk.z;
       const uint32_t buf = ug % kBufs2;
@@ -771,6 +775,8 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volat
     const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
     rows[0] = ra.x; rows[1] = ra.y; rows[2] = ra.z; rows[3] = ra.w;
     rows[4] = rb.x; rows[5] = rb.y; rows[6] = rb.z; rows[7] = rb.w;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) rows[k] = dbg_row(rows[k], a.pcap, a.status);
     // planes of each slot's pair row: the GEMM2 segments of its unit (block = row / 16, slice h)
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + h) : 0;
@@ -973,6 +979,8 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.sink = sink;
   a.plane_elems = (size_t)L.pcap * kHidden;
   a.T = T;
+  a.pcap = L.pcap;
+  a.e_local = L.e_local;
   a.f32_out = f32_out ? 1 : 0;
   const bool expire = test_expire_grid_wait();
   a.grid_extra = expire ? 1 : 0;

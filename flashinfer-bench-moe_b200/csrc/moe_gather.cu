@@ -23,7 +23,8 @@ __global__ void __launch_bounds__(kWarps * 32) gather_rows_kernel(const uint8_t*
                                                                   const int32_t* __restrict__ expert_poff_end,
                                                                   const int32_t* __restrict__ row_token,
                                                                   uint8_t* __restrict__ a_perm,
-                                                                  float* __restrict__ a_scale_perm, int pcap) {
+                                                                  float* __restrict__ a_scale_perm, int pcap,
+                                                                  uint32_t* __restrict__ status) {
   const int lane = threadIdx.x & 31;
   pdl_wait();
   pdl_trigger();
@@ -31,7 +32,7 @@ __global__ void __launch_bounds__(kWarps * 32) gather_rows_kernel(const uint8_t*
   // a warp per group of 32 rows: the scales with lane = row (coalesced stores),
   // then the 32 activation rows one after another
   for (int r0 = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * 32; r0 < rows; r0 += gridDim.x * kWarps * 32) {
-    const int my_tok = r0 + lane < rows ? row_token[r0 + lane] : -1;
+    const int my_tok = r0 + lane < rows ? dbg_row(row_token[r0 + lane], T, status) : -1;
     for (int kb = 0; kb < kHBlocks; ++kb)
       if (r0 + lane < rows)
         a_scale_perm[(size_t)kb * pcap + r0 + lane] = my_tok >= 0 ? __ldg(hidden_scale + (size_t)kb * T + my_tok) : 0.0f;
@@ -56,7 +57,8 @@ cudaError_t launch_gather_rows(const uint8_t* hidden, const float* hidden_scale,
   return launch_pdl(gather_rows_kernel, dim3(blocks), dim3(kWarps * 32), 0, stream, hidden, hidden_scale, T,
                     reinterpret_cast<const int32_t*>(ws + L.expert_poff) + L.e_local,
                     reinterpret_cast<const int32_t*>(ws + L.row_token), ws + L.a_perm,
-                    reinterpret_cast<float*>(ws + L.a_scale_perm), L.pcap);
+                    reinterpret_cast<float*>(ws + L.a_scale_perm), L.pcap,
+                    reinterpret_cast<uint32_t*>(ws + L.status));
 }
 
 }  // namespace fbmoe

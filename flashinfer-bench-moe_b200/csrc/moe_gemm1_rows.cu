@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_ascale, const float* __restrict__ w1_scale,
                       const int32_t* __restrict__ n_blocks_ptr, const int4* __restrict__ blocks,
                       __half* __restrict__ inter,
-                      uint32_t* __restrict__ status) {
+                      uint32_t* __restrict__ status, int e_local, int pcap) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = sm + kOffA;
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued_mask = 0, parity_mask = 0;  // per stage: ever issued / parity of the last issue
     int x = 0, ui = 0;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ui) {
-      const int4 blk = blocks[u / kTiles];
+      const int4 blk = dbg_block(blocks[u / kTiles], kRows, e_local, pcap, status);
       const int j = u % kTiles;
       const int e = blk.x, r0 = blk.y;
       const int wrow = e * kGemm1N + 128 * j;
@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int ui = 0;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ui) {
-      const int4 blk = blocks[u / kTiles];
+      const int4 blk = dbg_block(blocks[u / kTiles], kRows, e_local, pcap, status);
       const int j = u % kTiles;
       const int r0 = blk.y, nrows = blk.z;
       // this unit's W1 scales: [0, 56) first half, [56, 112) second half
@@ -327,7 +327,8 @@ cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_ap
   if (grid < 1) grid = 1;
   return launch_pdl(gemm1_rows_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, *tm_w1, *tm_aperm,
                     *tm_ascale, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
-                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<__half*>(ws + L.inter), reinterpret_cast<uint32_t*>(ws + L.status));
+                    reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<__half*>(ws + L.inter),
+                    reinterpret_cast<uint32_t*>(ws + L.status), L.e_local, L.pcap);
 }
 
 }  // namespace fbmoe

@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const int4* __restrict__ blocks, const float* __restrict__ row_weight,
                       __half* __restrict__ pair_out, uint32_t* __restrict__ status,
                       const int32_t* __restrict__ row_token, const int32_t* __restrict__ token_rows,
-                      const PeerScatter ps) {
+                      const PeerScatter ps, int T, int e_local, int pcap) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sRaw = sm + kOffRaw;
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       uint32_t issued_mask = 0, parity_mask = 0;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const int4 blk = blocks[u / kNTiles];
+        const int4 blk = dbg_block(blocks[u / kNTiles], kRows, e_local, pcap, status);
         const int nt = u % kNTiles;
         for (int ks = 0; ks < kKSteps; ++ks) {
           if (!mbar_wait(&emptyb[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Ring rr(kRawStages), cr(kConvStages);
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-      const int4 blk = blocks[u / kNTiles];
+      const int4 blk = dbg_block(blocks[u / kNTiles], kRows, e_local, pcap, status);
       const int nt = u % kNTiles;
       const float* s_lo = w2_scale + ((size_t)blk.x * kHBlocks + 2 * nt) * kIBlocks;  // rows 0..127
       const float* s_hi = s_lo + kIBlocks;                                           // rows 128..255
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ug = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ug) {
-      const int4 blk = blocks[u / kNTiles];
+      const int4 blk = dbg_block(blocks[u / kNTiles], kRows, e_local, pcap, status);
       const int nt = u % kNTiles;
       const int r0 = blk.y, nrows = blk.z;
       const float* s_lo = w2_scale + ((size_t)blk.x * kHBlocks + 2 * nt) * kIBlocks;
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool has_dst = row < nrows;
       if (ps.world > 0 && has_dst) {
         const int r = r0 + row;
-        const int t = __ldg(row_token + r);
+        const int t = dbg_token(__ldg(row_token + r), T, status);
         const int4* tr4 = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
         const int4 ra = __ldg(tr4), rb = __ldg(tr4 + 1);
         const int k = ra.x == r ? 0 : ra.y == r ? 1 : ra.z == r ? 2 : ra.w == r ? 3
@@ -397,7 +397,7 @@ cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm
                     reinterpret_cast<const int32_t*>(ws + L.n_blocks), reinterpret_cast<const int4*>(ws + L.blocks),
                     reinterpret_cast<const float*>(ws + L.row_weight), reinterpret_cast<__half*>(ws + L.pair_out),
                     reinterpret_cast<uint32_t*>(ws + L.status), reinterpret_cast<const int32_t*>(ws + L.row_token),
-                    reinterpret_cast<const int32_t*>(ws + L.token_rows), ps);
+                    reinterpret_cast<const int32_t*>(ws + L.token_rows), ps, L.tokens, L.e_local, L.pcap);
 }
 
 }  // namespace fbmoe

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __
                                                                 void* __restrict__ out_,
                                                                 const int32_t* __restrict__ splits,
                                                                 size_t plane_elems, uint32_t* status,
-                                                                uint32_t* sink) {
+                                                                uint32_t* sink, int pcap) {
   pdl_wait();
   // the last kernel of the call: every earlier kernel's status bits are visible now
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) forward_status_to_sink(status, sink);
@@ -31,7 +31,9 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_kernel(const __half* __
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
   const int4* rows4 = reinterpret_cast<const int4*>(token_rows + (size_t)t * kTopK);
   const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
-  const int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+  int rows[kTopK] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) rows[k] = dbg_row(rows[k], pcap, status);
   const int planes = splits[1];  // GEMM2 K splits: one plane of pair rows each
   for (int s = 0; s < planes; ++s)
 #pragma unroll
@@ -77,9 +79,9 @@ cudaError_t launch_reduce(int T, const Layout& L, uint8_t* ws, void* out, bool f
   uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
   if (f32_out)
     return launch_pdl(reduce_kernel<true>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane,
-                      status, sink);
+                      status, sink, L.pcap);
   return launch_pdl(reduce_kernel<false>, grid, dim3(kReduceThreads), 0, stream, pairs, rows, out, splits, plane,
-                    status, sink);
+                    status, sink, L.pcap);
 }
 
 }  // namespace fbmoe
