@@ -306,7 +306,8 @@ def run_ours(args, world, rank, local):
         # near 1430 MHz for a few seconds; latency-bound decode calls timed then run
         # up to 20 % slower.  Let the clock recover, and record it for every sweep.
         time.sleep(SWEEP_SETTLE_S)
-        for key, fn in (("decode_sweep", decode_sweep), ("quantiser", quantiser_point), ("prefill", prefill_points)):
+        for key, fn in (("decode_sweep", decode_sweep), ("quantiser", quantiser_point), ("prefill", prefill_points),
+                        ("prepack", prepack_points)):
             with ClockSampler(local, interval_s=0.05) as sweep_clk:
                 line[key] = fn(peaks)
             line[key]["clocks"] = sweep_clk.summary()
@@ -524,6 +525,29 @@ def prefill_points(peaks):
     return {"config": "config2 prefill, +3.0 bias on 4 local experts, 32 local experts",
             "peak_note": "fp8 peak = 2x measured bf16 burst; mixed peak weights GEMM1 fp8 and GEMM2 f16 by FLOPs",
             "points": res}
+
+
+def prepack_points(peaks):
+    """Offline W1 pre-pack (fbmoe_prepack_w1): the same calls on raw and on pre-packed W1, timed alternately on the
+    same inputs (config 1 decode at T = 1, 8, 64; config 2 prefill at T = 4096, 8192), L2 flushed between calls."""
+    import fbmoe_lib as L
+    import fbmoe_workloads as W
+    weights = W.make_weights(32, 4242, "cuda")
+    packed = L.prepack_w1(weights[0])
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    res = []
+    for T, cfg, iters in ((1, "standard", 30), (8, "standard", 30), (64, "standard", 30), (4096, "skew", 10),
+                          (8192, "skew", 10)):
+        inp = W.make_inputs(T, seed=T, config=cfg, device="cuda", weights=weights)
+        raw_args = W.as_args(inp)
+        pk_args = list(raw_args)
+        pk_args[4] = packed
+        raw = time_calls(lambda: L.forward(*raw_args, check=False), iters, lambda: flush_l2(buf))
+        pk = time_calls(lambda: L.forward(*pk_args, check=False, w1_packed=True), iters, lambda: flush_l2(buf))
+        res.append({"T": T, "config": cfg, "raw_us": round(raw * 1e3, 2), "prepacked_us": round(pk * 1e3, 2),
+                    "speedup": round(raw / pk, 4)})
+    del packed, weights
+    return {"what": "forward on raw W1 vs on fbmoe_prepack_w1 layout (one TMA box per GEMM1 tile)", "points": res}
 
 
 # --------------------------------------------------------------------------- CPU baselines

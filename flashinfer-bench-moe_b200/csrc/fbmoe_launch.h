@@ -142,7 +142,7 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
 cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
-                          uint32_t* sink, cudaStream_t stream);
+                          uint32_t* sink, bool w1_packed, cudaStream_t stream);
 // 0: no decode launch yet; 1: cooperative with programmatic serialization;
 // 2: cooperative; 3: plain programmatic launch sized by the occupancy query.
 int decode_launch_mode();
@@ -158,8 +158,10 @@ bool test_expire_grid_wait();
 constexpr uint64_t kTestGridWaitNs = 2000000ull;
 
 // GEMM1 + SwiGLU for blocks of 128 rows with the tokens as the MMA M operand.
+// w1_packed: tm_w1 maps the fbmoe_prepack_w1 layout with 256-row boxes (one box per
+// operand tile) instead of the raw layout with 64-row boxes.
 cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
-                              const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
+                              const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms, bool w1_packed,
                               cudaStream_t stream);
 
 // GEMM2 for blocks of 128 rows with the tokens as the MMA M operand; tm_w2raw
@@ -181,6 +183,6 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
                  size_t workspace_bytes, void* stream, bool allow_split = true,
                  const PeerScatter* scatter = nullptr, const int32_t* routed_idx = nullptr,
-                 const float* routed_w = nullptr);
+                 const float* routed_w = nullptr, bool w1_packed = false);
 
 }  // namespace fbmoe

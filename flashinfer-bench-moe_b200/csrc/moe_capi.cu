@@ -213,7 +213,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
                  size_t workspace_bytes, void* stream_, bool allow_split, const PeerScatter* scatter,
-                 const int32_t* routed_idx, const float* routed_w) {
+                 const int32_t* routed_idx, const float* routed_w, bool w1_packed) {
   if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
   const bool scattering = scatter != nullptr && scatter->world > 0;
@@ -237,8 +237,11 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   uint32_t* sink = status_sink_for(workspace);
 
   CUtensorMap tm_w1, tm_w2, tm_inter, tm_w2raw, tm_aperm, tm_ascale;
+  // raw W1: 64-row boxes (a tile is 2 or 4 of them); pre-packed W1: one box per
+  // tile, 128 rows (decode) or 256 rows (prefill)
+  const uint32_t w1_box_rows = w1_packed ? (bn == 16 ? 128u : 256u) : 64u;
   int rc = encode_2d(&tm_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm1_weights, kHidden, (uint64_t)E_local * kGemm1N,
-                     128, 64);
+                     128, w1_box_rows);
   if (rc) return rc;
   rc = encode_2d(&tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 128,
                  128);
@@ -290,14 +293,15 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
     // decode: GEMM1, GEMM2 and the combine run as one kernel (its time is the
     // "gemm1" stage of the profile; "gemm2" and "combine" stay empty)
     e = launch_decode(&tm_w1, &tm_w2, &tm_inter, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale,
-                      T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, sink, stream);
+                      T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, sink, w1_packed,
+                      stream);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 3, stream);
     prof_record(fwd, 4, stream);
   } else {
     e = launch_gather_rows(reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, L, ws, stream);
     if (e != cudaSuccess) return from_cuda(e);
-    e = launch_gemm1_rows(&tm_w1, &tm_aperm, &tm_ascale, gemm1_weights_scale, L, ws, sms, stream);
+    e = launch_gemm1_rows(&tm_w1, &tm_aperm, &tm_ascale, gemm1_weights_scale, L, ws, sms, w1_packed, stream);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 3, stream);
     e = launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream,

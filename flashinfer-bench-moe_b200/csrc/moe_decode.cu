@@ -156,6 +156,7 @@ struct DecodeArgs {
   int T;
   int pcap;                // row capacity of the workspace (bounds of the debug checks)
   int e_local;
+  int w1_packed;           // W1 in the fbmoe_prepack_w1 layout (tm_w1 then has 128-row boxes)
   int f32_out;
   int grid_extra;          // arrivals the combine waits for beyond gridDim.x (0; 1 only under the test hook)
   uint64_t grid_wait_ns;   // budget of the grid arrival wait
@@ -300,8 +301,13 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[stage], kA1Bytes);
-          tma_load_2d(sA + stage * kA1Bytes, &a.tm_w1, &full[stage], kb * kBlk, wrow1, pol_w);
-          tma_load_2d(sA + stage * kA1Bytes + 64 * 128, &a.tm_w1, &full[stage], kb * kBlk, wrow2, pol_w);
+          if (a.w1_packed) {
+            // packed rows [128g, 128g + 128) = this slice of both halves, one box
+            tma_load_2d(sA + stage * kA1Bytes, &a.tm_w1, &full[stage], kb * kBlk, e * kGemm1N + 128 * g, pol_w);
+          } else {
+            tma_load_2d(sA + stage * kA1Bytes, &a.tm_w1, &full[stage], kb * kBlk, wrow1, pol_w);
+            tma_load_2d(sA + stage * kA1Bytes + 64 * 128, &a.tm_w1, &full[stage], kb * kBlk, wrow2, pol_w);
+          }
         }
         last_parity[stage] = phase;
         const uint32_t bdst = smem_u32(sB + stage * kB1Bytes);
@@ -951,7 +957,7 @@ int decode_launch_mode() { return g_decode_mode.load(std::memory_order_relaxed);
 cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
-                          uint32_t* sink, cudaStream_t stream) {
+                          uint32_t* sink, bool w1_packed, cudaStream_t stream) {
   static DeviceFlags attr_set;
   if (cudaError_t err = set_max_dynamic_smem(decode_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
   DecodeArgs a;
@@ -981,6 +987,7 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.T = T;
   a.pcap = L.pcap;
   a.e_local = L.e_local;
+  a.w1_packed = w1_packed ? 1 : 0;
   a.f32_out = f32_out ? 1 : 0;
   const bool expire = test_expire_grid_wait();
   a.grid_extra = expire ? 1 : 0;

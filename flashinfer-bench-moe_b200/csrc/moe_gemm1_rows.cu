@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_ascale, const float* __restrict__ w1_scale,
                       const int32_t* __restrict__ n_blocks_ptr, const int4* __restrict__ blocks,
                       __half* __restrict__ inter,
-                      uint32_t* __restrict__ status, int e_local, int pcap) {
+                      uint32_t* __restrict__ status, int e_local, int pcap, int w1_packed) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = sm + kOffA;
@@ -153,10 +153,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes);
           tma_load_2d_nohint(sA + stage * kABytes, &tm_aperm, &full[stage], kb * kBlk, r0);
           uint8_t* b = sB + stage * kBBytes;
-          tma_load_2d_nohint(b, &tm_w1, &full[stage], kb * kBlk, wrow);
-          tma_load_2d_nohint(b + 64 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + 64);
-          tma_load_2d_nohint(b + 128 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + kInter);
-          tma_load_2d_nohint(b + 192 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + kInter + 64);
+          if (w1_packed) {
+            // packed rows [256j, 256j + 256): X1 2j, X2 2j, X1 2j+1, X2 2j+1 (64 rows each), one box
+            tma_load_2d_nohint(b, &tm_w1, &full[stage], kb * kBlk, e * kGemm1N + 256 * j);
+          } else {
+            tma_load_2d_nohint(b, &tm_w1, &full[stage], kb * kBlk, wrow);
+            tma_load_2d_nohint(b + 64 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + 64);
+            tma_load_2d_nohint(b + 128 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + kInter);
+            tma_load_2d_nohint(b + 192 * 128, &tm_w1, &full[stage], kb * kBlk, wrow + kInter + 64);
+          }
         }
         issued_mask |= 1u << stage;
         parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
@@ -230,6 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g = (warp - 2) >> 2;     // output columns [32g, 32g+32) of the tile
     const int row = q * 32 + lane;     // token row in the block == TMEM lane
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // TMEM columns of this warp's 32 X1 and 32 X2 columns: raw layout X1 0-127 | X2 128-255;
+    // packed layout in 64-column runs X1 | X2 | X1 | X2
+    const uint32_t x1_col = w1_packed ? (uint32_t)((g >> 1) * 128 + (g & 1) * 32) : (uint32_t)(32 * g);
+    const uint32_t x2_col = w1_packed ? x1_col + 64u : (uint32_t)(128 + 32 * g);
     uint32_t kbg = 0;
     bool ok = true;
     int ui = 0;
@@ -266,13 +275,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t t0 = tmem_base + lane_base + buf * 256 + 32 * g;
+        const uint32_t t0 = tmem_base + lane_base + buf * 256;
         const uint64_t f1 = f32x2_pack(a_s * w_1, a_s * w_1), f2 = f32x2_pack(a_s * w_2, a_s * w_2);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           // chunks 0-1: first-half columns (f1); 2-3: second half (f2)
           uint64_t p[8];
-          tmem_ld16_pairs(t0 + (c < 2 ? 16 * c : 128 + 16 * (c - 2)), p);
+          tmem_ld16_pairs(t0 + (c < 2 ? x1_col + 16 * c : x2_col + 16 * (c - 2)), p);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 8; ++i) f32x2_fma(acc[8 * c + i], p[i], c < 2 ? f1 : f2);
@@ -318,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
-                              const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms,
+                              const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms, bool w1_packed,
                               cudaStream_t stream) {
   static DeviceFlags attr_set;
   if (cudaError_t err = set_max_dynamic_smem(gemm1_rows_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
@@ -328,7 +337,7 @@ cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_ap
   return launch_pdl(gemm1_rows_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, *tm_w1, *tm_aperm,
                     *tm_ascale, w1_scale, reinterpret_cast<const int32_t*>(ws + L.n_blocks),
                     reinterpret_cast<const int4*>(ws + L.blocks), reinterpret_cast<__half*>(ws + L.inter),
-                    reinterpret_cast<uint32_t*>(ws + L.status), L.e_local, L.pcap);
+                    reinterpret_cast<uint32_t*>(ws + L.status), L.e_local, L.pcap, w1_packed ? 1 : 0);
 }
 
 }  // namespace fbmoe

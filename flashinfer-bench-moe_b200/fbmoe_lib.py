@@ -72,6 +72,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_decode_launch_mode.restype = i32
         lib.fbmoe_test_expire_grid_wait.argtypes = [i32]
         lib.fbmoe_test_expire_grid_wait.restype = i32
+        lib.fbmoe_prepack_w1.argtypes = [vp, i32, vp, vp]
+        lib.fbmoe_prepack_w1.restype = i32
+        lib.fbmoe_forward_prepacked.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, sz, vp]
+        lib.fbmoe_forward_prepacked.restype = i32
         lib.fbmoe_error_string.argtypes = [i32]
         lib.fbmoe_error_string.restype = ctypes.c_char_p
         lib.fbmoe_version.argtypes = []
@@ -276,7 +280,7 @@ def check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scal
 def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
             gemm2_weights, gemm2_weights_scale, local_expert_offset, routed_scaling_factor,
             out: torch.Tensor = None, workspace: torch.Tensor = None, check: bool = True,
-            partial_f32: bool = False, sync_status: bool = None) -> torch.Tensor:
+            partial_f32: bool = False, sync_status: bool = None, w1_packed: bool = False) -> torch.Tensor:
     """Run the fused MoE on the current stream; returns bf16 [T, 7168] (a fresh tensor unless `out` is given).
 
     With ``partial_f32`` the un-rounded fp32 sum over the local experts is returned
@@ -287,7 +291,9 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
     call's last kernel stores a non-zero status word into the workspace's pinned
     sink, and the next call on the same workspace (or check_status()) raises.
     ``sync_status=True`` (or FBMOE_SYNC_STATUS=1) synchronises the stream after
-    the launch and raises for this call itself."""
+    the launch and raises for this call itself.
+
+    ``w1_packed``: ``gemm1_weights`` is in the prepack_w1() layout (bf16 output only)."""
     lib = load_library()
     if check:
         T, E = check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
@@ -310,7 +316,9 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         word = _take_sink(key)
         if word:
             raise DeviceStatusError(word, "reported by an earlier forward on this stream's workspace")
-    fn = lib.fbmoe_forward_partial_f32 if partial_f32 else lib.fbmoe_forward
+    _require(not (w1_packed and partial_f32), "w1_packed supports the bf16 output only")
+    fn = lib.fbmoe_forward_partial_f32 if partial_f32 else (
+        lib.fbmoe_forward_prepacked if w1_packed else lib.fbmoe_forward)
     _check(fn(
         routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
         gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(), gemm2_weights.data_ptr(),
@@ -324,6 +332,19 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         if word:
             raise DeviceStatusError(word, "reported by this forward")
     return out
+
+
+def prepack_w1(gemm1_weights: torch.Tensor) -> torch.Tensor:
+    """W1 [E_local, 4096, 7168] e4m3 -> the same weights with the linear and silu halves interleaved in 64-row
+    slices (fbmoe_prepack_w1), for ``forward(..., w1_packed=True)``.  Runs on the current stream."""
+    _require(gemm1_weights.is_cuda and gemm1_weights.dtype == torch.float8_e4m3fn and gemm1_weights.is_contiguous()
+             and gemm1_weights.dim() == 3 and tuple(gemm1_weights.shape[1:]) == (2 * I, H),
+             "gemm1_weights must be a contiguous CUDA float8_e4m3fn tensor [E_local, 4096, 7168]")
+    packed = torch.empty_like(gemm1_weights)
+    stream = torch.cuda.current_stream(gemm1_weights.device).cuda_stream
+    _check(load_library().fbmoe_prepack_w1(gemm1_weights.data_ptr(), int(gemm1_weights.size(0)), packed.data_ptr(),
+                                           stream))
+    return packed
 
 
 def profile_begin(max_forwards: int) -> None:

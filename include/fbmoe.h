@@ -113,6 +113,25 @@ FBMOE_API int fbmoe_forward_noalloc(const float* routing_logits, const void* rou
  * looks up the array's address. */
 FBMOE_API int fbmoe_noalloc_read_status(uint32_t* status, void* stream);
 
+/* Offline weight pre-pack (no counterpart in the reference, which passes raw
+ * weights on every call, main.py:2720-2730).  Writes W1 [E_local, 4096, 7168]
+ * e4m3 with its linear half (rows 0..2047) and its silu half (rows 2048..4095)
+ * interleaved in 64-row slices: packed rows [128s, 128s+64) = rows [64s, 64s+64)
+ * and packed rows [128s+64, 128s+128) = rows [2048+64s, 2048+64s+64).  GEMM1 then
+ * loads each operand tile as one TMA box (128 rows at decode, 256 at prefill)
+ * instead of two or four.  The scales keep their layout.  `packed` must not
+ * overlap `gemm1_weights`; asynchronous on `stream`. */
+FBMOE_API int fbmoe_prepack_w1(const void* gemm1_weights, int E_local, void* packed, void* stream);
+
+/* fbmoe_forward with gemm1_weights in the fbmoe_prepack_w1 layout; the result is
+ * bit-identical to fbmoe_forward on the raw weights. */
+FBMOE_API int fbmoe_forward_prepacked(const float* routing_logits, const void* routing_bias,
+                                      const void* hidden_states, const float* hidden_states_scale,
+                                      const void* gemm1_weights_packed, const float* gemm1_weights_scale,
+                                      const void* gemm2_weights, const float* gemm2_weights_scale, int T,
+                                      int E_local, int local_expert_offset, float routed_scaling_factor, void* out,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* DeepSeek-V3 no-aux routing only (reference main.py:2522-2553 / fusedGatingKernel
  * main.py:851-1038).  topk_idx int32 [T, 8] global expert ids in canonical order
  * (descending s+bias, ascending id among equals); topk_weights fp32 [T, 8]. */
