@@ -267,6 +267,15 @@ __device__ __forceinline__ void tma_load_2d_nohint(void* smem_dst, const CUtenso
       : "memory");
 }
 
+// Prefetch one tile of a tensor map into L2 (no shared-memory destination and no
+// completion to wait for).  x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // L2 eviction policies (createpolicy).
 // 1-D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16),
 // completing as transaction bytes on `bar`.

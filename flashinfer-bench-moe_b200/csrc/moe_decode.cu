@@ -100,22 +100,30 @@ constexpr int kP1End = kP1Tok + BN * 4;
 // rows: 12 raw stages (192 KB of W2 in flight per SM).  Tensor memory: 16 GEMM2
 // accumulators of 16 columns (columns 0-255) and 4 converted stages of 64
 // columns (a 128-row x 128-K f16 tile, two K values per column; columns 256-511).
-constexpr int kRawStages = 12;
+constexpr int kRawStages = 9;
+// W2 tiles of its GEMM2 range a CTA asks L2 for when it has issued its last W1
+// load (384 KB per CTA, 57 MB over 148 CTAs: well inside the 126 MB L2), so
+// that HBM keeps streaming through the GEMM1 fix-ups and the hand-off to GEMM2.
+constexpr int kW2Prefetch = 24;
 constexpr int kConvStages = 4;
 constexpr int kConvGroups = 3;              // converter groups of 4 warps: {4-7}, {12-15}, {16-19}
-constexpr int kBStages = 4;
+
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
-constexpr int kB2Bytes = BN * 256;          // f16 intermediate rows (two 64-K halves)
+// The block's whole intermediate (16 rows x 2048 f16 = 64 KB) stays in shared
+// memory while the CTA works on that block's units: 32 chunks of 64 K-columns
+// (16 rows x 128 bytes, 128-byte swizzle), loaded once per block.
+constexpr int kInterChunkBytes = BN * 128;
+constexpr int kInterBytes = (kInter / 64) * kInterChunkBytes;
 constexpr int kBufs2 = 16;
 constexpr int kA2Col = kBufs2 * BN;         // first TMEM column of the converted stages
 constexpr int kA2StageCols = 64;
 constexpr int kP2Raw = 0;
-constexpr int kP2B = kP2Raw + kRawStages * kRawBytes;
-constexpr int kP2End = kP2B + kBStages * kB2Bytes;
+constexpr int kP2Inter = kP2Raw + kRawStages * kRawBytes;
+constexpr int kP2End = kP2Inter + kInterBytes;
 constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
 // ---- barriers and flags (not reused across phases)
 constexpr int kNumBars1 = 2 * kStages1 + 2 * kBufs1 + 1;
-constexpr int kNumBars2 = 2 * kRawStages + 2 * kConvStages + 2 * kBStages + 2 * kBufs2 + 1;
+constexpr int kNumBars2 = 2 * kRawStages + 2 * kConvStages + 2 + 2 * kBufs2 + 1;
 constexpr int kOffBar = kRegion;
 constexpr int kOffMisc = kOffBar + (kNumBars1 + kNumBars2) * 8;
 constexpr int kSmemBytes = kOffMisc + 32 + 1024;  // + alignment slack
@@ -332,6 +340,19 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         }
       }
     }
+    // GEMM2 streams this CTA's W2 tiles next: ask L2 for the first of them now.
+    if (lane == 0 && ok) {
+      const Partition P2 = gemm2_partition(nb, a.streamk != 0);
+      const int y_beg = P2.begin(blockIdx.x);
+      const int y_end = min(P2.begin(blockIdx.x + 1), y_beg + kW2Prefetch);
+      for (int y = y_beg; y < y_end;) {
+        const Seg sg = seg_at(P2, y, y_end);
+        y += sg.kb1 - sg.kb0;
+        const int4 blk = dbg_block(a.blocks[sg.u / kG2Slices], BN, a.e_local, a.pcap, a.status);
+        const int row = blk.x * kHidden + (sg.u % kG2Slices) * 128;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) tma_prefetch_l2_2d(&a.tm_w2, kb * kBlk, row);
+      }
+    }
     // complete the last kLag stages (or fewer)
     cp_async_wait_all();
     fence_proxy_async_smem();
@@ -518,16 +539,16 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 // ============================================================== GEMM2 phase
 __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
                                             int nb, volatile int* sAbort) {
-  constexpr int SR = kRawStages, SC = kConvStages, SB = kBStages;
+  constexpr int SR = kRawStages, SC = kConvStages;
   uint8_t* sRaw = sm + kP2Raw;
-  uint8_t* sB = sm + kP2B;
+  uint8_t* sInter = sm + kP2Inter;
   uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
   uint64_t* raw_empty = bars + SR;             // converters done reading it
   uint64_t* a_full = bars + 2 * SR;            // f16 W2 tile written by the converters
   uint64_t* c_empty = bars + 2 * SR + SC;      // MMA done with the converted slot
-  uint64_t* b_full = bars + 2 * SR + 2 * SC;   // intermediate rows landed (TMA)
-  uint64_t* b_empty = b_full + SB;             // MMA done with the intermediate slot
-  uint64_t* tfull = b_empty + SB;
+  uint64_t* inter_full = bars + 2 * SR + 2 * SC;  // a block's intermediate landed (TMA)
+  uint64_t* inter_empty = inter_full + 1;         // MMA done with the loaded block (another follows)
+  uint64_t* tfull = inter_full + 2;
   uint64_t* tempty = tfull + kBufs2;
   uint64_t* drain = tempty + kBufs2;
   const int warp = threadIdx.x >> 5;
@@ -544,14 +565,13 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     if (lane == 0) {
       const bool w2_side = (warp == 0);
       const uint64_t pol = w2_side ? l2_policy_evict_first() : l2_policy_evict_last();
-      const int n = w2_side ? SR : SB;
-      uint64_t* fullb = w2_side ? raw_full : b_full;
-      uint64_t* emptyb = w2_side ? raw_empty : b_empty;
-      Ring ring(n);
+      const int n = w2_side ? SR : 0;
+      Ring ring(SR);
       bool ok = true;
-      int ready_blk = -1;  // block whose intermediate rows are known complete
-      uint32_t last_parity[SR > SB ? SR : SB];
-      for (int s = 0; s < n; ++s) last_parity[s] = 0xFFFFFFFFu;
+      int ready_blk = -1;  // block whose intermediate rows are loaded
+      int nloads = 0;      // blocks loaded so far (intermediate side)
+      uint32_t last_parity[SR];
+      for (int s = 0; s < SR; ++s) last_parity[s] = 0xFFFFFFFFu;
       for (int x = x_beg; x < x_end && ok;) {
         const Seg sg = seg_at(P, x, x_end);
         x += sg.kb1 - sg.kb0;
@@ -561,6 +581,12 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         const int h = u % kG2Slices;
         const int e = blk.x, r0 = blk.y;
         if (!w2_side && b != ready_blk) {
+          // the MMAs on the previously loaded block are complete before its chunks are overwritten
+          if (nloads > 0 && !mbar_wait(inter_empty, (uint32_t)(nloads - 1) & 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutProducer);
+            break;
+          }
           // wait until GEMM1 published all 32 slices of this block's rows
           const uint64_t t0 = globaltimer_ns();
           while (ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
@@ -573,24 +599,23 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           }
           if (!ok) break;
           fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
+          // the block's whole intermediate: 32 chunks of 64 K-columns
+          mbar_arrive_expect_tx(inter_full, kInterBytes);
+          for (int c = 0; c < kInter / 64; ++c)
+            tma_load_2d(sInter + c * kInterChunkBytes, &a.tm_inter, inter_full, c * 64, r0, pol);
+          ++nloads;
           ready_blk = b;
         }
+        if (!w2_side) continue;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
-          if (!mbar_wait(&emptyb[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
+          if (!mbar_wait(&raw_empty[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutProducer);
             break;
           }
-          if (w2_side) {
-            mbar_arrive_expect_tx(&fullb[ring.slot], kRawBytes);
-            tma_load_2d(sRaw + ring.slot * kRawBytes, &a.tm_w2, &fullb[ring.slot], kb * kBlk, e * kHidden + h * 128,
-                        pol);
-          } else {
-            uint8_t* bb = sB + ring.slot * kB2Bytes;
-            mbar_arrive_expect_tx(&fullb[ring.slot], kB2Bytes);
-            tma_load_2d(bb, &a.tm_inter, &fullb[ring.slot], kb * kBlk, r0, pol);
-            tma_load_2d(bb + BN * 128, &a.tm_inter, &fullb[ring.slot], kb * kBlk + 64, r0, pol);
-          }
+          mbar_arrive_expect_tx(&raw_full[ring.slot], kRawBytes);
+          tma_load_2d(sRaw + ring.slot * kRawBytes, &a.tm_w2, &raw_full[ring.slot], kb * kBlk, e * kHidden + h * 128,
+                      pol);
           last_parity[ring.slot] = ring.phase;
           ring.next();
         }
@@ -598,21 +623,34 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       // every issued TMA load lands before the CTA exits
       for (int s = 0; s < n; ++s)
         if (last_parity[s] != 0xFFFFFFFFu)
-          if (!mbar_wait_drain(&fullb[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
+          if (!mbar_wait_drain(&raw_full[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
+      if (nloads > 0 && !mbar_wait_drain(inter_full, (uint32_t)(nloads - 1) & 1u, kWaitBudgetNs))
+        fail(kStatusTimeoutDrain);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, BN);  // f16 x f16
-      Ring ring(SC), bring(SB);
+      Ring ring(SC);
       uint32_t ug = 0;
       bool ok = true;
       bool any = false;
+      int cur_blk = -1, nloads = 0;
       for (int x = x_beg; x < x_end && ok; ++ug) {
         const Seg sg = seg_at(P, x, x_end);
         x += sg.kb1 - sg.kb0;
         const int nk = sg.kb1 - sg.kb0;
+        const int b = sg.u / kG2Slices;
+        if (b != cur_blk) {
+          if (!mbar_wait(inter_full, (uint32_t)nloads & 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          ++nloads;
+          cur_blk = b;
+        }
         const uint32_t buf = ug % kBufs2;
         if (!mbar_wait(&tempty[buf], ((ug / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
@@ -622,30 +660,29 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs) ||
-              !mbar_wait(&b_full[bring.slot], bring.phase, sAbort, kWaitBudgetNs)) {
+          if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
           }
           tc_fence_after();
-          // A: the converted stage in TMEM (K = 16 per MMA = 8 columns); B: the two
-          // 64-K halves of the intermediate rows in shared memory
+          // A: the converted stage in TMEM (K = 16 per MMA = 8 columns); B: the K-block's
+          // two 64-K chunks of the resident intermediate in shared memory
           const uint32_t a_col = tmem_base + kA2Col + ring.slot * kA2StageCols;
+          const uint8_t* bk = sInter + 2 * (sg.kb0 + kb) * kInterChunkBytes;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const uint64_t bdesc =
-                umma_desc_sw128(smem_u32(sB + bring.slot * kB2Bytes + (j >> 2) * BN * 128)) + 2 * (j & 3);
+            const uint64_t bdesc = umma_desc_sw128(smem_u32(bk + (j >> 2) * kInterChunkBytes)) + 2 * (j & 3);
             mma_f16_tmem_a(d, a_col + 8 * j, bdesc, idesc, (kb | j) ? 1u : 0u);
           }
           tc_commit(&c_empty[ring.slot]);
-          tc_commit(&b_empty[bring.slot]);
           any = true;
           ring.next();
-          bring.next();
         }
         if (!ok) break;
         tc_commit(&tfull[buf]);
+        // another block follows in this CTA's range: release the loaded intermediate
+        if (x < x_end && seg_at(P, x, x_end).u / kG2Slices != b) tc_commit(inter_empty);
       }
       if (any) {
         tc_commit(drain);
@@ -885,11 +922,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       mbar_init(&b2[kConvStages + s], 1);
     }
     b2 += 2 * kConvStages;
-    for (int s = 0; s < kBStages; ++s) {
-      mbar_init(&b2[s], 1);
-      mbar_init(&b2[kBStages + s], 1);
-    }
-    b2 += 2 * kBStages;
+    mbar_init(&b2[0], 1);  // intermediate of a block landed (expect_tx arrive)
+    mbar_init(&b2[1], 1);  // MMA done with it (tcgen05.commit)
+    b2 += 2;
     for (int b = 0; b < kBufs2; ++b) {
       mbar_init(&b2[b], 1);
       mbar_init(&b2[kBufs2 + b], 4);
