@@ -1,0 +1,1065 @@
+// moe_decode.cu -- the expert computation of a decode-sized call (16-row
+// blocks, T <= 64) as ONE persistent kernel: GEMM1 + SwiGLU, GEMM2 x routing
+// weight and the per-token combine (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Reference counterparts: gemm1_kernel + act_quant_kernel (solution/triton/
+// main.py:41-223, 1426-1602), gemm2_kernel (main.py:433-600) and
+// reduce_add_kernel (main.py:1604-1714).  Per local expert e, permuted row r
+// (token t) and hidden column h:
+//     G1[r, n]    = sum_k A[t, k] * a_scale[k/128, t] * W1[e, n, k] * s1[e, n/128, k/128]
+//     inter[r, j] = silu(G1[r, 2048 + j]) * G1[r, j]                 (f16, clamped)
+//     pair[r, h]  = w[r] * sum_j inter[r, j] * W2[e, h, j] * s2[e, h/128, j/128]   (f16)
+//     out[t, h]   = sum over t's local slots of pair[r, h]            (fp32 sum, bf16)
+// The intermediate is stored as f16 (not re-quantised to FP8, and not bf16):
+// against the reference's fp32 intermediate, FP8 re-quantisation puts about 10%
+// of output elements outside atol 1e-2 / rtol 2e-2, bf16 leaves the worst element
+// at ~1.0x the tolerance, f16 at ~0.35x.  Values beyond the f16 range are clamped
+// to +-65504 and flagged in the status word (kStatusSaturated).
+//
+// Why one kernel.  At decode sizes the call streams the active experts' weights
+// (44 MB each) and little else; separate GEMM1 / GEMM2 / combine launches cost a
+// grid drain, a launch and a prologue each, and GEMM2 could not start streaming
+// W2 before the last GEMM1 CTA retired.  Here every CTA runs its GEMM1 work items,
+// then its GEMM2 items: W2 tiles stream in at once, and only the intermediate
+// rows of a block wait for that block's 32 GEMM1 slices (a per-block counter
+// that GEMM1 raises after publishing them).  The combine runs after one grid-wide
+// arrival (every CTA has written its pair rows) and is spread over all threads.
+// The grid is at most one CTA per SM with one CTA resident per SM, nothing in
+// GEMM1 waits on GEMM2 and every CTA reaches the grid arrival, so every wait
+// ends; every wait is also bounded in wall time.
+//
+// Orientation (swap-AB) in both GEMMs: weight rows are the MMA's M = 128 operand
+// and the <= 16 token rows of a block its N operand.
+//
+// GEMM1 phase.  Work unit = (block of 16 rows of one expert) x (slice g of 64
+// output columns); the A tile stacks W1 rows [64g, 64g+64) (h1 half) on rows
+// [2048+64g, 2048+64g+64) (silu half); the B tile gathers the block's token rows
+// with cp.async (no permuted copy of the activations).  Every 128-K block is
+// MMA'd into its own TMEM buffer and promoted by s1 * a_scale into fp32
+// registers (the per-128-K block scales are applied exactly).  Four sets of four
+// epilogue warps take the K-blocks kb = j (mod 4), so four K-blocks are in flight
+// in the epilogue; their partial sums are added in set order.  Work is balanced
+// "stream-K" style: the phase's K-blocks, flattened unit-major, are cut into one
+// contiguous range per CTA (see Partition); a unit cut by range boundaries is
+// computed in segments whose fp32 partials the segment that arrives last adds in
+// segment order (deterministic).
+// Warps: w0 producer (TMA + cp.async), w1 MMA issuer, w2-w3 idle, w4-w19 epilogue.
+//
+// GEMM2 phase.  Work unit = (block) x (slice h of 128 hidden columns): A = 128
+// W2 rows, dequantised on chip to f16 (one HMUL2 by the power-of-two-shifted
+// f16 scale, see w2_block_exponent) by the converter warps straight into
+// tensor memory, where the MMA reads it; B = the block's f16 intermediate rows
+// (TMA).  TMEM accumulates the whole K = 2048 (no promotion: the scale is in the
+// operand).  Stream-K as in GEMM1, with ranges of >= 16 K-blocks, so a unit has at
+// most two segments; segment s writes plane s of the pair rows and the combine
+// adds a unit's planes.
+// Converting a K-block (shared-memory loads, cvt + HMUL2, tcgen05.st, wait) takes
+// longer than streaming it, so three groups of four converter warps take the
+// K-blocks j = 0, 1, 2 (mod 3): three K-blocks are converted at once.
+// Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 intermediate producer (TMA),
+// w4-w7, w12-w15 and w16-w19 converter groups, w8-w11 epilogue, w3 idle; then all
+// threads combine.
+#include "fbmoe_common.cuh"
+#include "fbmoe_launch.h"
+
+namespace fbmoe {
+namespace {
+
+constexpr int BN = 16;                      // rows per block
+constexpr int kThreads = 640;               // 20 warps
+constexpr uint64_t kWaitBudgetNs = 4000000000ull;
+constexpr int kG1Slices = kInter / 64;      // 32 slices of 64 intermediate columns
+constexpr int kG2Slices = kHidden / 128;    // 56 slices of 128 hidden columns
+
+// ---- GEMM1 phase layout (offsets inside the shared region)
+constexpr int kSets = 4;                    // epilogue warp sets
+constexpr int kEpi1Threads = 128 * kSets;
+// TMEM partial buffers: all 512 columns, so the MMA can run up to 32 K-blocks
+// (two split-K items) ahead of the promotion epilogue, whose per-item fix-up
+// (partials to L2, fence, counter) would otherwise stall the weight stream.
+constexpr int kBufs1 = 32;
+// 10 stages = 160 KB of W1 in flight per SM: HBM streaming at ~2 us loaded latency
+// needs roughly 90 KB per SM, and more absorbs the latency spread.
+constexpr int kStages1 = 10;
+// A stage's cp.async row copies are signalled complete kLag stages after they
+// are issued, so up to kLag stages of row copies are in flight.
+constexpr int kLag = kStages1 - 2;
+constexpr int kA1Bytes = 128 * 128;
+constexpr int kB1Bytes = BN * 128;
+constexpr int kXchStride = BN + 1;
+constexpr int kP1A = 0;
+constexpr int kP1B = kP1A + kStages1 * kA1Bytes;
+constexpr int kP1AScale = kP1B + kStages1 * kB1Bytes;
+constexpr int kP1WScale = kP1AScale + kHBlocks * BN * 4;
+constexpr int kP1Xch = kP1WScale + 2 * kHBlocks * 4;
+constexpr int kP1Tok = kP1Xch + kSets * 128 * kXchStride * 4;
+constexpr int kP1End = kP1Tok + BN * 4;
+// ---- GEMM2 phase layout
+// The W2 tile is converted to f16 straight into tensor memory, where the MMA
+// reads its A operand, so shared memory holds only raw W2 and the intermediate
+// rows: 12 raw stages (192 KB of W2 in flight per SM).  Tensor memory: 16 GEMM2
+// accumulators of 16 columns (columns 0-255) and 4 converted stages of 64
+// columns (a 128-row x 128-K f16 tile, two K values per column; columns 256-511).
+constexpr int kRawStages = 9;
+// W2 tiles of its GEMM2 range a CTA asks L2 for when it has issued its last W1
+// load (384 KB per CTA, 57 MB over 148 CTAs: well inside the 126 MB L2), so
+// that HBM keeps streaming through the GEMM1 fix-ups and the hand-off to GEMM2.
+constexpr int kW2Prefetch = 24;
+constexpr int kConvStages = 4;
+constexpr int kConvGroups = 3;              // converter groups of 4 warps: {4-7}, {12-15}, {16-19}
+
+constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
+// The block's whole intermediate (16 rows x 2048 f16 = 64 KB) stays in shared
+// memory while the CTA works on that block's units: 32 chunks of 64 K-columns
+// (16 rows x 128 bytes, 128-byte swizzle), loaded once per block.
+constexpr int kInterChunkBytes = BN * 128;
+constexpr int kInterBytes = (kInter / 64) * kInterChunkBytes;
+constexpr int kBufs2 = 16;
+constexpr int kA2Col = kBufs2 * BN;         // first TMEM column of the converted stages
+constexpr int kA2StageCols = 64;
+constexpr int kP2Raw = 0;
+constexpr int kP2Inter = kP2Raw + kRawStages * kRawBytes;
+constexpr int kP2End = kP2Inter + kInterBytes;
+constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
+// ---- barriers and flags (not reused across phases)
+constexpr int kNumBars1 = 2 * kStages1 + 2 * kBufs1 + 1;
+constexpr int kNumBars2 = 2 * kRawStages + 2 * kConvStages + 2 + 2 * kBufs2 + 1;
+constexpr int kOffBar = kRegion;
+constexpr int kOffMisc = kOffBar + (kNumBars1 + kNumBars2) * 8;
+constexpr int kSmemBytes = kOffMisc + 32 + 1024;  // + alignment slack
+constexpr int kTmemCols = 512;                    // one CTA per SM holds all of TMEM
+static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
+static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
+// Every raw stage is converted by one group, and a group's previous c_empty wait
+// already covered the MMA of K-block j - kConvGroups - kConvStages >= j - 2 * kConvStages,
+// so no parity wait below can see a phase two completions old.
+static_assert(kRawStages % kConvGroups == 0 && kConvGroups <= kConvStages, "converter group schedule");
+static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
+static_assert(kBufs1 * BN <= kTmemCols && kA2Col + kConvStages * kA2StageCols <= kTmemCols, "TMEM allocation");
+
+struct DecodeArgs {
+  CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
+  CUtensorMap tm_w2;     // W2 rows x 2048 K, 128-byte x 128-row boxes
+  CUtensorMap tm_inter;  // inter rows x 2048 f16, 64-column x 16-row boxes
+  const uint8_t* hidden;
+  const float* hidden_scale;
+  const float* w1_scale;
+  const float* w2_scale;
+  const int32_t* n_blocks;
+  const int4* blocks;
+  const int32_t* row_token;
+  const float* row_weight;
+  const int32_t* token_rows;
+  int streamk;           // 1: K-block-granular partition with split-K fix-ups; 0: whole units
+  int32_t* split_count;
+  float* split_part;
+  int32_t* blk_ready;
+  int32_t* grid_sync;
+  __half* inter;
+  __half* pair_out;
+  void* out;
+  uint32_t* status;
+  uint32_t* sink;          // host-visible copy of a non-zero status word (nullptr: none)
+  size_t plane_elems;
+  int T;
+  int pcap;                // row capacity of the workspace (bounds of the debug checks)
+  int e_local;
+  int w1_packed;           // W1 in the fbmoe_prepack_w1 layout (tm_w1 then has 128-row boxes)
+  int f32_out;
+  int grid_extra;          // arrivals the combine waits for beyond gridDim.x (0; 1 only under the test hook)
+  uint64_t grid_wait_ns;   // budget of the grid arrival wait
+};
+
+// Ring position: slot and phase parity of successive uses of a ring of n slots.
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  int n;
+  __device__ explicit Ring(int n_) : n(n_) {}
+  __device__ void next() {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Balanced partition of one phase's K-blocks over the CTAs that take part
+// ("stream-K"): the phase's units are flattened unit-major (unit u holds K-blocks
+// [u*len, u*len + len)) and CTA c owns the range [begin(c), begin(c+1)).  A unit
+// cut by range boundaries is computed in segments on different CTAs and fixed up
+// in segment order (deterministic).  With unit_aligned the boundaries fall on
+// unit boundaries, so no unit is cut (used when no split-K buffers exist).
+struct Partition {
+  int total;         // units * len
+  int len;           // K-blocks per unit
+  int g;             // CTAs that take part
+  bool unit_aligned;
+  __device__ int begin(int c) const {
+    if (c >= g) return total;
+    if (unit_aligned) return (int)(((long long)c * (total / len)) / g) * len;
+    return (int)(((long long)c * total) / g);
+  }
+  // the CTA whose range holds K-block x
+  __device__ int owner(int x) const {
+    if (unit_aligned) {
+      const long long nu = total / len;
+      return (int)((((long long)(x / len) + 1) * g + nu - 1) / nu) - 1;
+    }
+    return (int)((((long long)x + 1) * g + total - 1) / total) - 1;
+  }
+  __device__ int first_owner(int u) const { return owner(u * len); }
+  __device__ int nseg(int u) const { return owner(u * len + len - 1) - owner(u * len) + 1; }
+};
+
+// The segment of unit x / len that starts at K-block x and ends before `end`.
+struct Seg {
+  int u, kb0, kb1;
+};
+__device__ __forceinline__ Seg seg_at(const Partition& P, int x, int end) {
+  Seg sg;
+  sg.u = x / P.len;
+  sg.kb0 = x % P.len;
+  sg.kb1 = min(P.len, sg.kb0 + (end - x));
+  return sg;
+}
+
+// Phase partitions.  Stream-K: GEMM1 ranges hold >= 8 K-blocks (a unit has up to 8
+// segments; a CTA writes at most 2 partials: its first and its last unit); GEMM2
+// ranges hold >= 16 K-blocks = one unit, so a unit has at most 2 segments = planes.
+__device__ __forceinline__ Partition gemm1_partition(int nb, bool streamk) {
+  const int units = nb * kG1Slices, total = units * kHBlocks;
+  const int g = streamk ? max(1, min((int)gridDim.x, total / 8)) : max(1, min((int)gridDim.x, units));
+  return Partition{total, kHBlocks, g, !streamk};
+}
+__device__ __forceinline__ Partition gemm2_partition(int nb, bool streamk) {
+  const int units = nb * kG2Slices, total = units * kIBlocks;
+  const int g = streamk ? max(1, min((int)gridDim.x, total / kIBlocks)) : max(1, min((int)gridDim.x, units));
+  return Partition{total, kIBlocks, g, !streamk};
+}
+// fp32 partial slot of CTA c's segment of unit u: 2c for its first unit, 2c + 1 for its last.
+__device__ __forceinline__ int partial_slot(const Partition& P, int c, int u) {
+  return 2 * c + (u == P.begin(c) / P.len ? 0 : 1);
+}
+
+// ============================================================== GEMM1 phase
+__device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
+                                            int nb, volatile int* sAbort, volatile int* sLast) {
+  constexpr int S = kStages1;
+  uint8_t* sA = sm + kP1A;
+  uint8_t* sB = sm + kP1B;
+  float* sAScale = reinterpret_cast<float*>(sm + kP1AScale);  // [56][BN]
+  float* sWScale = reinterpret_cast<float*>(sm + kP1WScale);  // [2][56]
+  float* sXch = reinterpret_cast<float*>(sm + kP1Xch);        // [sets][128][BN+1] partial sums
+  int* sTok = reinterpret_cast<int*>(sm + kP1Tok);            // [BN]
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = tfull + kBufs1;
+  uint64_t* drain = tempty + kBufs1;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const Partition P = gemm1_partition(nb, a.streamk != 0);
+  const int x_beg = P.begin(blockIdx.x), x_end = P.begin(blockIdx.x + 1);
+  auto fail = [&](uint32_t bit) {
+    *sAbort = 1;
+    atomicOr(a.status, bit);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol_w = l2_policy_evict_first();  // each weight tile is read about once
+    int stage = 0;
+    uint32_t phase = 0;
+    long issued = 0;
+    bool ok = true;
+    uint32_t last_parity[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) last_parity[s] = 0xFFFFFFFFu;
+    for (int x = x_beg; x < x_end && ok;) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u;
+      const int4 blk = dbg_block(a.blocks[u / kG1Slices], BN, a.e_local, a.pcap, a.status);
+      const int g = u % kG1Slices;
+      const int e = blk.x, r0 = blk.y, nrows = blk.z;
+      // token row pointers for the rows this lane copies: rows (lane>>3) + 4j
+      constexpr int kRowsPerLane = BN / 4;
+      const uint8_t* src[kRowsPerLane];
+#pragma unroll
+      for (int j = 0; j < kRowsPerLane; ++j) {
+        const int row = (lane >> 3) + 4 * j;
+        src[j] = (row < nrows) ? a.hidden + (size_t)dbg_token(a.row_token[r0 + row], a.T, a.status) * kHidden +
+                                     (lane & 7) * 16
+                               : a.hidden;
+      }
+      const int wrow1 = e * kGemm1N + 64 * g;
+      const int wrow2 = wrow1 + kInter;
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutProducer);
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], kA1Bytes);
+          if (a.w1_packed) {
+            // packed rows [128g, 128g + 128) = this slice of both halves, one box
+            tma_load_2d(sA + stage * kA1Bytes, &a.tm_w1, &full[stage], kb * kBlk, e * kGemm1N + 128 * g, pol_w);
+          } else {
+            tma_load_2d(sA + stage * kA1Bytes, &a.tm_w1, &full[stage], kb * kBlk, wrow1, pol_w);
+            tma_load_2d(sA + stage * kA1Bytes + 64 * 128, &a.tm_w1, &full[stage], kb * kBlk, wrow2, pol_w);
+          }
+        }
+        last_parity[stage] = phase;
+        const uint32_t bdst = smem_u32(sB + stage * kB1Bytes);
+#pragma unroll
+        for (int j = 0; j < kRowsPerLane; ++j) {
+          const int row = (lane >> 3) + 4 * j;
+          cp_async_16(bdst + sw128_offset(row, lane & 7), src[j] + kb * kBlk, row < nrows ? 16u : 0u);
+        }
+        cp_async_commit();
+        ++issued;
+        if (issued > kLag) {
+          cp_async_wait_group<kLag>();
+          fence_proxy_async_smem();
+          __syncwarp();
+          int ps = stage - kLag;
+          if (ps < 0) ps += S;
+          if (lane == 0) mbar_arrive(&full[ps]);
+        }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // GEMM2 streams this CTA's W2 tiles next: ask L2 for the first of them now.
+    if (lane == 0 && ok) {
+      const Partition P2 = gemm2_partition(nb, a.streamk != 0);
+      const int y_beg = P2.begin(blockIdx.x);
+      const int y_end = min(P2.begin(blockIdx.x + 1), y_beg + kW2Prefetch);
+      for (int y = y_beg; y < y_end;) {
+        const Seg sg = seg_at(P2, y, y_end);
+        y += sg.kb1 - sg.kb0;
+        const int4 blk = dbg_block(a.blocks[sg.u / kG2Slices], BN, a.e_local, a.pcap, a.status);
+        const int row = blk.x * kHidden + (sg.u % kG2Slices) * 128;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) tma_prefetch_l2_2d(&a.tm_w2, kb * kBlk, row);
+      }
+    }
+    // complete the last kLag stages (or fewer)
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const long tail = issued < kLag ? issued : kLag;
+      for (long i = tail; i >= 1; --i) {
+        int ps = stage - (int)i;
+        while (ps < 0) ps += S;
+        mbar_arrive(&full[ps]);
+      }
+      // drain: every issued TMA load must have landed before the smem is reused
+      for (int s = 0; s < S; ++s)
+        if (last_parity[s] != 0xFFFFFFFFu)
+          if (!mbar_wait_drain(&full[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(0u, 128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t kbg = 0;
+      bool ok = true;
+      bool any = false;
+      for (int x = x_beg; x < x_end && ok;) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        for (int l = 0; l < sg.kb1 - sg.kb0; ++l) {
+          const uint32_t buf = kbg % kBufs1;
+          if (!mbar_wait(&tempty[buf], ((kbg / kBufs1) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
+              !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * kA1Bytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * kB1Bytes));
+          const uint32_t d = tmem_base + buf * BN;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mma_f8f6f4(d, adesc + 2 * j, bdesc + 2 * j, idesc, j > 0 ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          tc_commit(&tfull[buf]);
+          any = true;
+          ++kbg;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (any) {
+        // all issued MMAs complete before TMEM and shared memory are reused
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0, kWaitBudgetNs);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    constexpr int G = kSets;
+    const int set = (warp - 4) >> 2;   // this warp's K-block residue class
+    const int ew = warp & 3;           // TMEM lane quarter
+    const int row = ew * 32 + lane;    // A row == TMEM lane
+    const int etid = threadIdx.x - 128;
+    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+    uint32_t kbg = 0;                  // K-blocks this CTA processed before the current item
+    bool ok = true;
+    for (int x = x_beg; x < x_end && ok;) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u, nk = sg.kb1 - sg.kb0;
+      const int nseg = P.nseg(u);
+      const int4 blk = dbg_block(a.blocks[u / kG1Slices], BN, a.e_local, a.pcap, a.status);
+      const int g = u % kG1Slices;
+      const int e = blk.x, r0 = blk.y, nrows = blk.z;
+      if (etid < BN) sTok[etid] = (etid < nrows) ? dbg_token(a.row_token[r0 + etid], a.T, a.status) : -1;
+      if (etid < 2 * kHBlocks) {
+        const int h = etid / kHBlocks, kb = etid % kHBlocks;
+        const int nbk = h * (kInter / kBlk) + g / 2;
+        sWScale[etid] = a.w1_scale[((size_t)e * (kGemm1N / kBlk) + nbk) * kHBlocks + kb];
+      }
+      named_barrier_sync(1, kEpi1Threads);
+      for (int i = etid; i < kHBlocks * BN; i += kEpi1Threads) {
+        const int kb = i / BN, t = i % BN;
+        const int tok = sTok[t];
+        sAScale[i] = tok >= 0 ? a.hidden_scale[(size_t)kb * a.T + tok] : 0.0f;
+      }
+      named_barrier_sync(1, kEpi1Threads);
+
+      float acc[BN];
+#pragma unroll
+      for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
+      const float* wsc = sWScale + (ew < 2 ? 0 : kHBlocks);
+      bool bad = false;
+      // this set takes the item's K-blocks whose CTA-wide index is = set (mod G)
+      for (int l = (set - (int)(kbg % G) + G) % G; l < nk; l += G) {
+        const uint32_t kgl = kbg + l;
+        const uint32_t buf = kgl % kBufs1;
+        if (!mbar_wait(&tfull[buf], (kgl / kBufs1) & 1u, sAbort, kWaitBudgetNs)) {
+          bad = true;
+          if (lane == 0) fail(kStatusTimeoutEpilogue);
+          break;
+        }
+        tc_fence_after();
+        const int kb = sg.kb0 + l;
+        const float ws = wsc[kb];
+        const float* asc = sAScale + kb * BN;
+        float p[16];
+        tmem_ld16(tmem_base + lane_base + buf * BN, p);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(p[i], ws * asc[i], acc[i]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+      }
+      kbg += nk;
+      // Each set publishes its partial sums; they are added in set order.
+      if (!bad) {
+        float* mine = sXch + (size_t)(set * 128 + row) * kXchStride;
+#pragma unroll
+        for (int t = 0; t < BN; ++t) mine[t] = acc[t];
+      }
+      if (named_barrier_or(1, kEpi1Threads, bad)) {
+        ok = false;
+        break;
+      }
+      bool last = true;
+      if (nseg > 1) {
+        // publish this segment's partial, then find out whether it completes the unit
+        float* part = a.split_part + (size_t)partial_slot(P, blockIdx.x, u) * 128 * BN;
+        for (int i = etid; i < 128 * BN; i += kEpi1Threads) {
+          const int r = i / BN, t = i % BN;
+          float v = 0.0f;
+#pragma unroll
+          for (int j = 0; j < G; ++j) v += sXch[(size_t)(j * 128 + r) * kXchStride + t];
+          part[i] = v;
+        }
+        __threadfence();
+        named_barrier_sync(1, kEpi1Threads);
+        if (etid == 0) *sLast = (atomicAdd(&a.split_count[u], 1) == nseg - 1) ? 1 : 0;
+        named_barrier_sync(1, kEpi1Threads);
+        last = *sLast != 0;
+        if (last) __threadfence();
+      }
+      if (last) {
+        // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).
+        const int c0 = P.first_owner(u);
+        for (int i = etid; i < 64 * BN; i += kEpi1Threads) {
+          const int r = i % 64, t = i / 64;
+          if (t < nrows) {
+            float x1 = 0.0f, x2 = 0.0f;
+            if (nseg == 1) {
+#pragma unroll
+              for (int j = 0; j < G; ++j) {
+                x1 += sXch[(size_t)(j * 128 + r) * kXchStride + t];
+                x2 += sXch[(size_t)(j * 128 + 64 + r) * kXchStride + t];
+              }
+            } else {
+              for (int q = 0; q < nseg; ++q) {  // segment order: deterministic
+                const float* pq = a.split_part + (size_t)partial_slot(P, c0 + q, u) * 128 * BN;
+                x1 += __ldcg(pq + r * BN + t);
+                x2 += __ldcg(pq + (64 + r) * BN + t);
+              }
+            }
+            bool sat = false;
+            const float silu = x2 / (1.0f + expf(-x2));
+            a.inter[(size_t)(r0 + t) * kInter + 64 * g + r] = to_half_sat(silu * x1, sat);
+            if (sat) atomicOr(a.status, kStatusSaturated);
+          }
+        }
+        if (nseg > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
+        __threadfence();  // the slice's rows are visible before the block counter moves
+      }
+      named_barrier_sync(1, kEpi1Threads);
+      // one more of this block's 32 slices is published (GEMM2 waits for all 32)
+      if (last && etid == 0) atomicAdd(&a.blk_ready[u / kG1Slices], 1);
+    }
+  }
+}
+
+// ============================================================== GEMM2 phase
+__device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
+                                            int nb, volatile int* sAbort) {
+  constexpr int SR = kRawStages, SC = kConvStages;
+  uint8_t* sRaw = sm + kP2Raw;
+  uint8_t* sInter = sm + kP2Inter;
+  uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
+  uint64_t* raw_empty = bars + SR;             // converters done reading it
+  uint64_t* a_full = bars + 2 * SR;            // f16 W2 tile written by the converters
+  uint64_t* c_empty = bars + 2 * SR + SC;      // MMA done with the converted slot
+  uint64_t* inter_full = bars + 2 * SR + 2 * SC;  // a block's intermediate landed (TMA)
+  uint64_t* inter_empty = inter_full + 1;         // MMA done with the loaded block (another follows)
+  uint64_t* tfull = inter_full + 2;
+  uint64_t* tempty = tfull + kBufs2;
+  uint64_t* drain = tempty + kBufs2;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const Partition P = gemm2_partition(nb, a.streamk != 0);
+  const int x_beg = P.begin(blockIdx.x), x_end = P.begin(blockIdx.x + 1);
+  auto fail = [&](uint32_t bit) {
+    *sAbort = 1;
+    atomicOr(a.status, bit);
+  };
+
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ producers
+    if (lane == 0) {
+      const bool w2_side = (warp == 0);
+      const uint64_t pol = w2_side ? l2_policy_evict_first() : l2_policy_evict_last();
+      const int n = w2_side ? SR : 0;
+      Ring ring(SR);
+      bool ok = true;
+      int ready_blk = -1;  // block whose intermediate rows are loaded
+      int nloads = 0;      // blocks loaded so far (intermediate side)
+      uint32_t last_parity[SR];
+      for (int s = 0; s < SR; ++s) last_parity[s] = 0xFFFFFFFFu;
+      for (int x = x_beg; x < x_end && ok;) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        const int u = sg.u;
+        const int b = u / kG2Slices;
+        const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
+        const int h = u % kG2Slices;
+        const int e = blk.x, r0 = blk.y;
+        if (!w2_side && b != ready_blk) {
+          // the MMAs on the previously loaded block are complete before its chunks are overwritten
+          if (nloads > 0 && !mbar_wait(inter_empty, (uint32_t)(nloads - 1) & 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutProducer);
+            break;
+          }
+          // wait until GEMM1 published all 32 slices of this block's rows
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
+            if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
+              ok = false;
+              fail(kStatusTimeoutProducer);
+              break;
+            }
+            __nanosleep(200);
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
+          // the block's whole intermediate: 32 chunks of 64 K-columns
+          mbar_arrive_expect_tx(inter_full, kInterBytes);
+          for (int c = 0; c < kInter / 64; ++c)
+            tma_load_2d(sInter + c * kInterChunkBytes, &a.tm_inter, inter_full, c * 64, r0, pol);
+          ++nloads;
+          ready_blk = b;
+        }
+        if (!w2_side) continue;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+          if (!mbar_wait(&raw_empty[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutProducer);
+            break;
+          }
+          mbar_arrive_expect_tx(&raw_full[ring.slot], kRawBytes);
+          tma_load_2d(sRaw + ring.slot * kRawBytes, &a.tm_w2, &raw_full[ring.slot], kb * kBlk, e * kHidden + h * 128,
+                      pol);
+          last_parity[ring.slot] = ring.phase;
+          ring.next();
+        }
+      }
+      // every issued TMA load lands before the CTA exits
+      for (int s = 0; s < n; ++s)
+        if (last_parity[s] != 0xFFFFFFFFu)
+          if (!mbar_wait_drain(&raw_full[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
+      if (nloads > 0 && !mbar_wait_drain(inter_full, (uint32_t)(nloads - 1) & 1u, kWaitBudgetNs))
+        fail(kStatusTimeoutDrain);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(0u, 128, BN);  // f16 x f16
+      Ring ring(SC);
+      uint32_t ug = 0;
+      bool ok = true;
+      bool any = false;
+      int cur_blk = -1, nloads = 0;
+      for (int x = x_beg; x < x_end && ok; ++ug) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        const int nk = sg.kb1 - sg.kb0;
+        const int b = sg.u / kG2Slices;
+        if (b != cur_blk) {
+          if (!mbar_wait(inter_full, (uint32_t)nloads & 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          ++nloads;
+          cur_blk = b;
+        }
+        const uint32_t buf = ug % kBufs2;
+        if (!mbar_wait(&tempty[buf], ((ug / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          fail(kStatusTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          tc_fence_after();
+          // A: the converted stage in TMEM (K = 16 per MMA = 8 columns); B: the K-block's
+          // two 64-K chunks of the resident intermediate in shared memory
+          const uint32_t a_col = tmem_base + kA2Col + ring.slot * kA2StageCols;
+          const uint8_t* bk = sInter + 2 * (sg.kb0 + kb) * kInterChunkBytes;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint64_t bdesc = umma_desc_sw128(smem_u32(bk + (j >> 2) * kInterChunkBytes)) + 2 * (j & 3);
+            mma_f16_tmem_a(d, a_col + 8 * j, bdesc, idesc, (kb | j) ? 1u : 0u);
+          }
+          tc_commit(&c_empty[ring.slot]);
+          any = true;
+          ring.next();
+        }
+        if (!ok) break;
+        tc_commit(&tfull[buf]);
+        // another block follows in this CTA's range: release the loaded intermediate
+        if (x < x_end && seg_at(P, x, x_end).u / kG2Slices != b) tc_commit(inter_empty);
+      }
+      if (any) {
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0, kWaitBudgetNs);
+      }
+    }
+    __syncwarp();
+  } else if ((warp >= 4 && warp < 8) || warp >= 12) {
+    // ------------------------------------------------------------ converters
+    // Group grp (warps 4-7, 12-15, 16-19) converts the CTA's K-blocks j with
+    // j % kConvGroups == grp.  Warp w converts rows 32 (w % 4) .. +31 (its TMEM
+    // lane quarter) of the K-block: 128 fp8 -> 64 columns of f16 pairs, one HMUL2
+    // per pair, written to the stage's TMEM columns with two tcgen05.st.
+    const int q4 = warp & 3;
+    const int grp = warp < 8 ? 0 : (warp - 8) >> 2;
+    const int r = q4 * 32 + lane;  // W2 row of the tile = TMEM lane
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(q4 * 32) << 16) + kA2Col;
+    int j = 0;  // the CTA's running K-block index in this phase
+    bool ok = true;
+    for (int x = x_beg; x < x_end && ok;) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int nk = sg.kb1 - sg.kb0;
+      const int first = (grp - j % kConvGroups + kConvGroups) % kConvGroups;  // this group's first K-block
+      if (first >= nk) {
+        j += nk;
+        continue;
+      }
+      const int u = sg.u;
+      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
+      const int h = u % kG2Slices;
+      const float* sc = a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
+      const int kexp = w2_block_exponent(sc);
+      // the unit's 16 scales, one per lane: no global load on the per-stage path
+      const float lane_scale = __ldg(sc + (lane & (kIBlocks - 1)));
+      for (int l = first; l < nk; l += kConvGroups) {
+        const int jj = j + l, kb = sg.kb0 + l;
+        const int rs = jj % SR, cs = jj % SC;
+        if (!mbar_wait(&raw_full[rs], (uint32_t)(jj / SR) & 1u, sAbort, kWaitBudgetNs) ||
+            !mbar_wait(&c_empty[cs], ((uint32_t)(jj / SC) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutConvert);
+          break;
+        }
+        tc_fence_after();  // the MMAs that read this TMEM stage have completed
+        const __half2 sc2 = __half2half2(__float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, kb), kexp)));
+        const uint8_t* raw = sRaw + rs * kRawBytes;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t o[32];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 qv = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, 4 * half + i));
+            const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[k] & 0xFFFFu), __NV_E4M3);
+              const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[k] >> 16), __NV_E4M3);
+              const __half2 pl = __hmul2(*reinterpret_cast<const __half2*>(&lo), sc2);
+              const __half2 ph = __hmul2(*reinterpret_cast<const __half2*>(&hi), sc2);
+              o[8 * i + 2 * k] = *reinterpret_cast<const uint32_t*>(&pl);
+              o[8 * i + 2 * k + 1] = *reinterpret_cast<const uint32_t*>(&ph);
+            }
+          }
+          tmem_st32(lane_addr + cs * kA2StageCols + 32 * half, o);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&raw_empty[rs]);
+          mbar_arrive(&a_full[cs]);
+        }
+      }
+      j += nk;
+    }
+  } else if (warp >= 8 && warp < 12) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 8;
+    const int hrow = ew * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+    uint32_t ug = 0;
+    for (int x = x_beg; x < x_end; ++ug) {
+      const Seg sg = seg_at(P, x, x_end);
+      x += sg.kb1 - sg.kb0;
+      const int u = sg.u;
+      const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
+      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
+      const int h = u % kG2Slices;
+      const int r0 = blk.y, nrows = blk.z;
+      const uint32_t buf = ug % kBufs2;
+      if (!mbar_wait(&tfull[buf], (ug / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
+        if (lane == 0) fail(kStatusTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
+      const float* wrow = a.row_weight + r0;
+      // the converters scaled W2 by 2^k (see w2_block_exponent): undo it exactly
+      const int kexp = w2_block_exponent(a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks);
+      bool sat = false;
+      float p[16];
+      tmem_ld16(tmem_base + lane_base + buf * BN, p);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < nrows) dst[(size_t)i * kHidden] = to_half_sat(p[i] * ldexpf(__ldg(wrow + i), -kexp), sat);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (sat) atomicOr(a.status, kStatusSaturated);
+    }
+  }
+}
+
+// ============================================================== combine phase
+// After every CTA has written its pair rows (one arrival each on a grid counter
+// that the permute kernel zeroed): out[t, 8c .. 8c+7] for every token t and
+// column group c, spread over all threads of the grid.  The token's pair rows are
+// summed over planes, then slots, in fixed order (deterministic), in fp32.
+__device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volatile int* sAbort) {
+  const Partition P2 = gemm2_partition(nb, a.streamk != 0);
+  constexpr int kGroupsPerRow = kHidden / 8;
+  const int tasks = a.T * kGroupsPerRow;
+  // consecutive tasks go to different CTAs, so a small T still uses many SMs
+  const int first = threadIdx.x * gridDim.x + blockIdx.x;
+  // A task's slot rows and plane counts depend only on the permutation, so the
+  // first task's are fetched while the grid arrival completes.
+  int rows[kTopK], np[kTopK];
+  auto prep = [&](int task) {
+    const int t = task / kGroupsPerRow, h = (task % kGroupsPerRow) * 8 / 128;
+    const int4* rows4 = reinterpret_cast<const int4*>(a.token_rows + (size_t)t * kTopK);
+    const int4 ra = __ldg(rows4), rb = __ldg(rows4 + 1);
+    rows[0] = ra.x; rows[1] = ra.y; rows[2] = ra.z; rows[3] = ra.w;
+    rows[4] = rb.x; rows[5] = rb.y; rows[6] = rb.z; rows[7] = rb.w;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) rows[k] = dbg_row(rows[k], a.pcap, a.status);
+    // planes of each slot's pair row: the GEMM2 segments of its unit (block = row / 16, slice h)
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + h) : 0;
+  };
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
+    atomicAdd(a.grid_sync, 1);
+  }
+  // the first task's slot rows load while the other CTAs arrive
+  if (first < tasks) prep(first);
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu(a.grid_sync) < (int)gridDim.x + a.grid_extra) {
+      if (globaltimer_ns() - t0 > a.grid_wait_ns) {
+        *sAbort = 1;
+        atomicOr(a.status, kStatusTimeoutEpilogue);
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+  __syncthreads();
+  if (*sAbort) return;
+  for (int task = first; task < tasks; task += gridDim.x * kThreads) {
+    if (task != first) prep(task);
+    const int t = task / kGroupsPerRow;
+    const size_t col = (size_t)(task % kGroupsPerRow) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int pl = 0; pl < 2; ++pl) {  // planes, then slots: fixed order
+      // the plane's (up to 8) rows are loaded together: one L2 round trip per plane
+      uint4 v[kTopK];
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k)
+        v[k] = pl < np[k] ? __ldcg(reinterpret_cast<const uint4*>(a.pair_out + (size_t)pl * a.plane_elems +
+                                                                  (size_t)rows[k] * kHidden + col))
+                          : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        if (pl < np[k]) {
+          const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          }
+        }
+      }
+    }
+    if (a.f32_out) {
+      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + (size_t)t * kHidden + col);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 bv = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        ow[i] = *reinterpret_cast<const uint32_t*>(&bv);
+      }
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)t * kHidden + col) = o;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars1 = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint64_t* bars2 = bars1 + kNumBars1;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sm + kOffMisc + 4);
+  volatile int* sLast = reinterpret_cast<volatile int*>(sm + kOffMisc + 8);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    // phase 1: full/empty [8], tfull/tempty [32], drain
+    for (int s = 0; s < kStages1; ++s) {
+      mbar_init(&bars1[s], 2);               // producer expect_tx arrive + cp.async completion arrive
+      mbar_init(&bars1[kStages1 + s], 1);    // tcgen05.commit
+    }
+    for (int b = 0; b < kBufs1; ++b) {
+      mbar_init(&bars1[2 * kStages1 + b], 1);           // tcgen05.commit
+      mbar_init(&bars1[2 * kStages1 + kBufs1 + b], 4);  // one arrive per warp of the owning set
+    }
+    mbar_init(&bars1[2 * kStages1 + 2 * kBufs1], 1);
+    // phase 2: raw full/empty, converted full/empty, intermediate full/empty, tfull/tempty, drain
+    uint64_t* b2 = bars2;
+    for (int s = 0; s < kRawStages; ++s) {
+      mbar_init(&b2[s], 1);
+      mbar_init(&b2[kRawStages + s], 4);  // one arrive per warp of the converting group
+    }
+    b2 += 2 * kRawStages;
+    for (int s = 0; s < kConvStages; ++s) {
+      mbar_init(&b2[s], 4);
+      mbar_init(&b2[kConvStages + s], 1);
+    }
+    b2 += 2 * kConvStages;
+    mbar_init(&b2[0], 1);  // intermediate of a block landed (expect_tx arrive)
+    mbar_init(&b2[1], 1);  // MMA done with it (tcgen05.commit)
+    b2 += 2;
+    for (int b = 0; b < kBufs2; ++b) {
+      mbar_init(&b2[b], 1);
+      mbar_init(&b2[kBufs2 + b], 4);
+    }
+    mbar_init(&b2[2 * kBufs2], 1);
+    *sAbort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&a.tm_w1);
+    tma_prefetch_desc(&a.tm_w2);
+    tma_prefetch_desc(&a.tm_inter);
+  }
+  if (warp == 1) {
+    tmem_alloc(sTmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
+  fence_proxy_async_global();
+  const uint32_t tmem_base = *sTmem;
+  const int nb = *a.n_blocks;
+
+  if (nb == 0) {
+    // no local (token, expert) pair: the output is all zeros
+    const size_t n16 = (size_t)a.T * kHidden * (a.f32_out ? 4 : 2) / 16;
+    uint4* o = reinterpret_cast<uint4*>(a.out);
+    for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n16; i += (size_t)gridDim.x * kThreads)
+      o[i] = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    gemm1_phase(a, sm, bars1, tmem_base, nb, sAbort, sLast);
+    // The shared region changes role: order this CTA's generic-proxy accesses of
+    // phase 1 before the TMA writes of phase 2, and phase 1's TMEM reads before
+    // phase 2's MMAs.
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (!*sAbort) gemm2_phase(a, sm, bars2, tmem_base, nb, sAbort);
+    __syncthreads();  // this CTA's pair rows are all written
+    combine_phase(a, nb, sAbort);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  // The decode kernel is the last of the call: a status bit set by any kernel of
+  // the call (this CTA's included, ordered by the barrier above) reaches the sink.
+  if (threadIdx.x == 0) forward_status_to_sink(a.status, a.sink);
+}
+
+}  // namespace
+
+// How the decode kernel was last launched (fbmoe_decode_launch_mode).
+static std::atomic<int> g_decode_mode{0};
+
+int decode_launch_mode() { return g_decode_mode.load(std::memory_order_relaxed); }
+
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
+                          const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
+                          const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
+                          uint32_t* sink, bool w1_packed, cudaStream_t stream) {
+  static DeviceFlags attr_set;
+  if (cudaError_t err = set_max_dynamic_smem(decode_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
+  DecodeArgs a;
+  a.tm_w1 = *tm_w1;
+  a.tm_w2 = *tm_w2;
+  a.tm_inter = *tm_inter;
+  a.hidden = hidden;
+  a.hidden_scale = hidden_scale;
+  a.w1_scale = w1_scale;
+  a.w2_scale = w2_scale;
+  a.n_blocks = reinterpret_cast<const int32_t*>(ws + L.n_blocks);
+  a.blocks = reinterpret_cast<const int4*>(ws + L.blocks);
+  a.row_token = reinterpret_cast<const int32_t*>(ws + L.row_token);
+  a.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
+  a.token_rows = reinterpret_cast<const int32_t*>(ws + L.token_rows);
+  a.streamk = L.split_items > 0 ? 1 : 0;
+  a.split_count = reinterpret_cast<int32_t*>(ws + L.split_count);
+  a.split_part = reinterpret_cast<float*>(ws + L.split_part);
+  a.blk_ready = reinterpret_cast<int32_t*>(ws + L.blk_ready);
+  a.grid_sync = reinterpret_cast<int32_t*>(ws + L.grid_sync);
+  a.inter = reinterpret_cast<__half*>(ws + L.inter);
+  a.pair_out = reinterpret_cast<__half*>(ws + L.pair_out);
+  a.out = out;
+  a.status = reinterpret_cast<uint32_t*>(ws + L.status);
+  a.sink = sink;
+  a.plane_elems = (size_t)L.pcap * kHidden;
+  a.T = T;
+  a.pcap = L.pcap;
+  a.e_local = L.e_local;
+  a.w1_packed = w1_packed ? 1 : 0;
+  a.f32_out = f32_out ? 1 : 0;
+  const bool expire = test_expire_grid_wait();
+  a.grid_extra = expire ? 1 : 0;
+  a.grid_wait_ns = expire ? kTestGridWaitNs : kWaitBudgetNs;
+  // Every CTA waits at the grid arrival for all the others, so the whole grid
+  // must be resident at once: one CTA per SM (the occupancy query confirms that
+  // one fits), launched cooperatively so that the launch itself guarantees it
+  // even when other work holds SMs.  The first launch on a device tries the
+  // cooperative launch with programmatic serialization, then without it; if the
+  // driver refuses both, the grid falls back to a plain launch sized by the
+  // occupancy query (the arrival wait is bounded either way).
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel, kThreads, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  if (occ < 1) return cudaErrorInvalidConfiguration;
+  const int grid = num_sms > 0 ? num_sms : 1;
+  const int mode = g_decode_mode.load(std::memory_order_relaxed);
+  if (mode == 0 || mode == 1) {
+    e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, true, a);
+    if (e == cudaSuccess) {
+      g_decode_mode.store(1, std::memory_order_relaxed);
+      return e;
+    }
+    if (mode == 1) return e;
+    (void)cudaGetLastError();  // a refused launch configuration is not a sticky error
+  }
+  if (mode == 0 || mode == 2) {
+    e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, false, a);
+    if (e == cudaSuccess) {
+      g_decode_mode.store(2, std::memory_order_relaxed);
+      return e;
+    }
+    if (mode == 2) return e;
+    (void)cudaGetLastError();
+  }
+  g_decode_mode.store(3, std::memory_order_relaxed);
+  return launch_pdl(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, a);
+}
+
+}  // namespace fbmoe
