@@ -277,21 +277,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t t0 = tmem_base + lane_base + buf * 256;
         const uint64_t f1 = f32x2_pack(a_s * w_1, a_s * w_1), f2 = f32x2_pack(a_s * w_2, a_s * w_2);
-        // two 32-column loads (X1, then X2): two TMEM round trips per K-block; the
-        // buffer goes back to the MMA as soon as both halves are in registers, before
-        // the X2 multiply-adds
-        uint64_t p[16];
-        tmem_ld32_pairs(t0 + x1_col, p);
-        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) f32x2_fma(acc[i], p[i], f1);
-        tmem_ld32_pairs(t0 + x2_col, p);
-        tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          // chunks 0-1: first-half columns (f1); 2-3: second half (f2)
+          uint64_t p[8];
+          tmem_ld16_pairs(t0 + (c < 2 ? x1_col + 16 * c : x2_col + 16 * (c - 2)), p);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f32x2_fma(acc[8 * c + i], p[i], c < 2 ? f1 : f2);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) f32x2_fma(acc[16 + i], p[i], f2);
         ++kbg;
       }
       if (!ok) break;

@@ -11,14 +11,6 @@
 // One warp per (row, 8 consecutive blocks): 128 bf16 = 8 bytes per lane per
 // block, warp max by shuffles, one 4-byte store per lane per block.  HBM-bound:
 // 14,336 B read + 7,168 B + 224 B written per row.
-//
-// Division.  An IEEE fp32 division per element made the kernel issue-bound (about
-// 20 instructions each).  The quotient only matters up to its e4m3 rounding, so
-// each element is first computed as y = x * (1/s) (two roundings, within 1.5 fp32
-// ulp of the exact quotient).  Unless y lies within 4 ulp of an e4m3 rounding
-// midpoint (low 20 mantissa bits near 0x80000) or in the e4m3 subnormal range
-// (|y| < 2^-6), y and the correctly rounded x / s round to the same e4m3 value;
-// in those rare cases the element is recomputed with the exact division.
 #include "fbmoe.h"
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
@@ -60,16 +52,12 @@ __global__ void __launch_bounds__(kWarps * 32) quant_act_kernel(const __nv_bfloa
 #pragma unroll
     for (int j = 0; j < kGroup; ++j) {
       const float s = m[j] > 0.0f ? __fdiv_rn(m[j], 448.0f) : 1.0f;
-      const float r = __frcp_rn(s);
       const float v[4] = {__uint_as_float(raw[j].x << 16), __uint_as_float(raw[j].x & 0xFFFF0000u),
                           __uint_as_float(raw[j].y << 16), __uint_as_float(raw[j].y & 0xFFFF0000u)};
       uint32_t packed = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float y = __fmul_rn(v[i], r);
-        const uint32_t low = __float_as_uint(y) & 0xFFFFFu;
-        if (fabsf(y) < 0.015625f || (low > 0x80000u - 4u && low < 0x80000u + 4u)) y = __fdiv_rn(v[i], s);
-        y = fminf(fmaxf(y, -448.0f), 448.0f);
+        const float y = fminf(fmaxf(__fdiv_rn(v[i], s), -448.0f), 448.0f);
         packed |= (uint32_t)__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3) << (8 * i);
       }
       *reinterpret_cast<uint32_t*>(q + base + j * kBlk) = packed;
