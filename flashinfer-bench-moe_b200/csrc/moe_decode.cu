@@ -95,47 +95,39 @@ constexpr int kP1Xch = kP1WScale + 2 * kHBlocks * 4;
 constexpr int kP1Tok = kP1Xch + kSets * 128 * kXchStride * 4;
 constexpr int kP1End = kP1Tok + BN * 4;
 // ---- GEMM2 phase layout
-// The W2 tile is converted to f16 straight into tensor memory, where the MMA
-// reads its A operand, so shared memory holds only raw W2 and the intermediate
-// rows: 12 raw stages (192 KB of W2 in flight per SM).  Tensor memory: 16 GEMM2
-// accumulators of 16 columns (columns 0-255) and 4 converted stages of 64
-// columns (a 128-row x 128-K f16 tile, two K values per column; columns 256-511).
+// A = the W2 tile (fp8, 128 rows x 128 K) from a TMA ring; B = the block's
+// intermediate as two fp8 planes (see gemm2_phase), resident in shared memory
+// for all of the CTA's units of that block: per K-block 32 rows (plane 0 then
+// plane 1, 16 token rows each) x 128 bytes, 128-byte swizzle, plus the planes'
+// fp32 scales.  Tensor memory: 16 accumulator buffers of 32 columns.
 constexpr int kRawStages = 9;
 // W2 tiles of its GEMM2 range a CTA asks L2 for when it has issued its last W1
 // load (384 KB per CTA, 57 MB over 148 CTAs: well inside the 126 MB L2), so
 // that HBM keeps streaming through the GEMM1 fix-ups and the hand-off to GEMM2.
 constexpr int kW2Prefetch = 24;
-constexpr int kConvStages = 4;
-constexpr int kConvGroups = 3;              // converter groups of 4 warps: {4-7}, {12-15}, {16-19}
-
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
-// The block's whole intermediate (16 rows x 2048 f16 = 64 KB) stays in shared
-// memory while the CTA works on that block's units: 32 chunks of 64 K-columns
-// (16 rows x 128 bytes, 128-byte swizzle), loaded once per block.
-constexpr int kInterChunkBytes = BN * 128;
-constexpr int kInterBytes = (kInter / 64) * kInterChunkBytes;
+constexpr int kPlaneRows = 2 * BN;          // two planes of BN token rows
+constexpr int kPlaneKBytes = kPlaneRows * 128;
 constexpr int kBufs2 = 16;
-constexpr int kA2Col = kBufs2 * BN;         // first TMEM column of the converted stages
-constexpr int kA2StageCols = 64;
+constexpr int kCols2 = kPlaneRows;          // accumulator columns per buffer
+constexpr int kEpi2Threads = 512;           // warps 4-19
 constexpr int kP2Raw = 0;
-constexpr int kP2Inter = kP2Raw + kRawStages * kRawBytes;
-constexpr int kP2End = kP2Inter + kInterBytes;
+constexpr int kP2Planes = kP2Raw + kRawStages * kRawBytes;
+constexpr int kP2PScale = kP2Planes + kIBlocks * kPlaneKBytes;
+constexpr int kP2End = kP2PScale + kIBlocks * kPlaneRows * 4;
 constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
 // ---- barriers and flags (not reused across phases)
 constexpr int kNumBars1 = 2 * kStages1 + 2 * kBufs1 + 1;
-constexpr int kNumBars2 = 2 * kRawStages + 2 * kConvStages + 2 + 2 * kBufs2 + 1;
+constexpr int kNumBars2 = 2 * kRawStages + 2 + 2 * kBufs2 + 1;
 constexpr int kOffBar = kRegion;
 constexpr int kOffMisc = kOffBar + (kNumBars1 + kNumBars2) * 8;
 constexpr int kSmemBytes = kOffMisc + 32 + 1024;  // + alignment slack
 constexpr int kTmemCols = 512;                    // one CTA per SM holds all of TMEM
 static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
 static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
-// Every raw stage is converted by one group, and a group's previous c_empty wait
-// already covered the MMA of K-block j - kConvGroups - kConvStages >= j - 2 * kConvStages,
-// so no parity wait below can see a phase two completions old.
-static_assert(kRawStages % kConvGroups == 0 && kConvGroups <= kConvStages, "converter group schedule");
 static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
-static_assert(kBufs1 * BN <= kTmemCols && kA2Col + kConvStages * kA2StageCols <= kTmemCols, "TMEM allocation");
+static_assert(kBufs1 * BN <= kTmemCols && kBufs2 * kCols2 <= kTmemCols, "TMEM allocation");
+static_assert(kP2Planes % 1024 == 0, "the planes are 128-byte swizzle atoms");
 
 struct DecodeArgs {
   CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
@@ -537,18 +529,39 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 }
 
 // ============================================================== GEMM2 phase
+// The intermediate of a block (<= 16 token rows x 2048, f16 from GEMM1) is
+// split into two fp8 planes with their own scales per (token row, 128-K block):
+//     s0 = amax|x| / 448,  q0 = e4m3(x / s0),  r = x - q0 * s0,
+//     s1 = amax|r| / 448,  q1 = e4m3(r / s1),  x ~ q0 * s0 + q1 * s1
+// (the same 1x128 rule as the activations, applied twice).  GEMM2 then runs as
+// kind::f8f6f4 straight on the fp8 W2 tile, with no dequantisation of W2: per
+// K-block one MMA chain of N = 32 (both planes) into a TMEM buffer, promoted by
+// the W2 block scale times each plane's scale:
+//     acc[t] += s2[h, kb] * (s0[t, kb] * D[:, t] + s1[t, kb] * D[:, 16 + t])
+// W2 itself enters exactly (fp8 times its fp32 scale), and two planes keep about
+// eight significant bits of every intermediate value relative to its block's
+// largest; measured on the host against the fp32 intermediate, the worst pair-row
+// element is within 0.13x the output tolerance, against 0.08x for the f16
+// intermediate with f16 W2 this replaces (and 0.40x for bf16, 5.8x for one fp8
+// plane).
+//
+// Warps: w0 W2 producer (TMA ring), w1 MMA issuer, w4-w19 build the planes of
+// each new block together (after the block's 32 GEMM1 slices are published and
+// the MMAs on the previous block's planes have completed), then promote: a unit's
+// K-blocks are promoted by one set of four warps (units go to the sets round
+// robin), which at the unit's end multiplies by the routing weight and stores the
+// f16 pair rows of its segment's plane.
 __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
                                             int nb, volatile int* sAbort) {
-  constexpr int SR = kRawStages, SC = kConvStages;
+  constexpr int SR = kRawStages;
   uint8_t* sRaw = sm + kP2Raw;
-  uint8_t* sInter = sm + kP2Inter;
-  uint64_t* raw_full = bars;                   // raw W2 tile landed (TMA)
-  uint64_t* raw_empty = bars + SR;             // converters done reading it
-  uint64_t* a_full = bars + 2 * SR;            // f16 W2 tile written by the converters
-  uint64_t* c_empty = bars + 2 * SR + SC;      // MMA done with the converted slot
-  uint64_t* inter_full = bars + 2 * SR + 2 * SC;  // a block's intermediate landed (TMA)
-  uint64_t* inter_empty = inter_full + 1;         // MMA done with the loaded block (another follows)
-  uint64_t* tfull = inter_full + 2;
+  uint8_t* sPlanes = sm + kP2Planes;
+  float* sPScale = reinterpret_cast<float*>(sm + kP2PScale);  // [16 K-blocks][32 plane rows]
+  uint64_t* raw_full = bars;                  // W2 tile landed (TMA)
+  uint64_t* raw_empty = bars + SR;            // MMA done with it (tcgen05.commit)
+  uint64_t* planes_full = bars + 2 * SR;      // the block's planes are written (one arrive)
+  uint64_t* planes_empty = planes_full + 1;   // MMA done with them (another block follows)
+  uint64_t* tfull = planes_full + 2;
   uint64_t* tempty = tfull + kBufs2;
   uint64_t* drain = tempty + kBufs2;
   const int warp = threadIdx.x >> 5;
@@ -560,53 +573,19 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     atomicOr(a.status, bit);
   };
 
-  if (warp == 0 || warp == 2) {
-    // ------------------------------------------------------------ producers
+  if (warp == 0) {
+    // ------------------------------------------------------------ W2 producer
     if (lane == 0) {
-      const bool w2_side = (warp == 0);
-      const uint64_t pol = w2_side ? l2_policy_evict_first() : l2_policy_evict_last();
-      const int n = w2_side ? SR : 0;
+      const uint64_t pol = l2_policy_evict_first();
       Ring ring(SR);
       bool ok = true;
-      int ready_blk = -1;  // block whose intermediate rows are loaded
-      int nloads = 0;      // blocks loaded so far (intermediate side)
       uint32_t last_parity[SR];
       for (int s = 0; s < SR; ++s) last_parity[s] = 0xFFFFFFFFu;
       for (int x = x_beg; x < x_end && ok;) {
         const Seg sg = seg_at(P, x, x_end);
         x += sg.kb1 - sg.kb0;
-        const int u = sg.u;
-        const int b = u / kG2Slices;
-        const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
-        const int h = u % kG2Slices;
-        const int e = blk.x, r0 = blk.y;
-        if (!w2_side && b != ready_blk) {
-          // the MMAs on the previously loaded block are complete before its chunks are overwritten
-          if (nloads > 0 && !mbar_wait(inter_empty, (uint32_t)(nloads - 1) & 1u, sAbort, kWaitBudgetNs)) {
-            ok = false;
-            fail(kStatusTimeoutProducer);
-            break;
-          }
-          // wait until GEMM1 published all 32 slices of this block's rows
-          const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
-            if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
-              ok = false;
-              fail(kStatusTimeoutProducer);
-              break;
-            }
-            __nanosleep(200);
-          }
-          if (!ok) break;
-          fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
-          // the block's whole intermediate: 32 chunks of 64 K-columns
-          mbar_arrive_expect_tx(inter_full, kInterBytes);
-          for (int c = 0; c < kInter / 64; ++c)
-            tma_load_2d(sInter + c * kInterChunkBytes, &a.tm_inter, inter_full, c * 64, r0, pol);
-          ++nloads;
-          ready_blk = b;
-        }
-        if (!w2_side) continue;
+        const int4 blk = dbg_block(a.blocks[sg.u / kG2Slices], BN, a.e_local, a.pcap, a.status);
+        const int wrow = blk.x * kHidden + (sg.u % kG2Slices) * 128;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&raw_empty[ring.slot], ring.phase ^ 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
@@ -614,75 +593,61 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
             break;
           }
           mbar_arrive_expect_tx(&raw_full[ring.slot], kRawBytes);
-          tma_load_2d(sRaw + ring.slot * kRawBytes, &a.tm_w2, &raw_full[ring.slot], kb * kBlk, e * kHidden + h * 128,
-                      pol);
+          tma_load_2d(sRaw + ring.slot * kRawBytes, &a.tm_w2, &raw_full[ring.slot], kb * kBlk, wrow, pol);
           last_parity[ring.slot] = ring.phase;
           ring.next();
         }
       }
       // every issued TMA load lands before the CTA exits
-      for (int s = 0; s < n; ++s)
+      for (int s = 0; s < SR; ++s)
         if (last_parity[s] != 0xFFFFFFFFu)
           if (!mbar_wait_drain(&raw_full[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
-      if (nloads > 0 && !mbar_wait_drain(inter_full, (uint32_t)(nloads - 1) & 1u, kWaitBudgetNs))
-        fail(kStatusTimeoutDrain);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc(0u, 128, BN);  // f16 x f16
-      Ring ring(SC);
-      uint32_t ug = 0;
+      constexpr uint32_t idesc = umma_idesc(0u, 128, kCols2);  // e4m3 x e4m3
+      Ring ring(SR);
+      uint32_t kgl = 0;
+      int cur_blk = -1, nblk = 0;
       bool ok = true;
       bool any = false;
-      int cur_blk = -1, nloads = 0;
-      for (int x = x_beg; x < x_end && ok; ++ug) {
+      for (int x = x_beg; x < x_end && ok;) {
         const Seg sg = seg_at(P, x, x_end);
         x += sg.kb1 - sg.kb0;
-        const int nk = sg.kb1 - sg.kb0;
         const int b = sg.u / kG2Slices;
         if (b != cur_blk) {
-          if (!mbar_wait(inter_full, (uint32_t)nloads & 1u, sAbort, kWaitBudgetNs)) {
+          if (!mbar_wait(planes_full, (uint32_t)nblk & 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
           }
-          ++nloads;
+          ++nblk;
           cur_blk = b;
         }
-        const uint32_t buf = ug % kBufs2;
-        if (!mbar_wait(&tempty[buf], ((ug / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
-          ok = false;
-          fail(kStatusTimeoutMma);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem_base + buf * BN;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&a_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++kgl) {
+          const uint32_t buf = kgl % kBufs2;
+          if (!mbar_wait(&tempty[buf], ((kgl / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
+              !mbar_wait(&raw_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
           }
           tc_fence_after();
-          // A: the converted stage in TMEM (K = 16 per MMA = 8 columns); B: the K-block's
-          // two 64-K chunks of the resident intermediate in shared memory
-          const uint32_t a_col = tmem_base + kA2Col + ring.slot * kA2StageCols;
-          const uint8_t* bk = sInter + 2 * (sg.kb0 + kb) * kInterChunkBytes;
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sRaw + ring.slot * kRawBytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sPlanes + kb * kPlaneKBytes));
+          const uint32_t d = tmem_base + buf * kCols2;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint64_t bdesc = umma_desc_sw128(smem_u32(bk + (j >> 2) * kInterChunkBytes)) + 2 * (j & 3);
-            mma_f16_tmem_a(d, a_col + 8 * j, bdesc, idesc, (kb | j) ? 1u : 0u);
-          }
-          tc_commit(&c_empty[ring.slot]);
+          for (int j = 0; j < 4; ++j) mma_f8f6f4(d, adesc + 2 * j, bdesc + 2 * j, idesc, j > 0 ? 1u : 0u);
+          tc_commit(&raw_empty[ring.slot]);
+          tc_commit(&tfull[buf]);
           any = true;
           ring.next();
         }
         if (!ok) break;
-        tc_commit(&tfull[buf]);
-        // another block follows in this CTA's range: release the loaded intermediate
-        if (x < x_end && seg_at(P, x, x_end).u / kG2Slices != b) tc_commit(inter_empty);
+        // another block follows in this CTA's range: release the planes once these MMAs complete
+        if (x < x_end && seg_at(P, x, x_end).u / kG2Slices != b) tc_commit(planes_empty);
       }
       if (any) {
         tc_commit(drain);
@@ -690,110 +655,137 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       }
     }
     __syncwarp();
-  } else if ((warp >= 4 && warp < 8) || warp >= 12) {
-    // ------------------------------------------------------------ converters
-    // Group grp (warps 4-7, 12-15, 16-19) converts the CTA's K-blocks j with
-    // j % kConvGroups == grp.  Warp w converts rows 32 (w % 4) .. +31 (its TMEM
-    // lane quarter) of the K-block: 128 fp8 -> 64 columns of f16 pairs, one HMUL2
-    // per pair, written to the stage's TMEM columns with two tcgen05.st.
-    const int q4 = warp & 3;
-    const int grp = warp < 8 ? 0 : (warp - 8) >> 2;
-    const int r = q4 * 32 + lane;  // W2 row of the tile = TMEM lane
-    const uint32_t lane_addr = tmem_base + ((uint32_t)(q4 * 32) << 16) + kA2Col;
-    int j = 0;  // the CTA's running K-block index in this phase
-    bool ok = true;
-    for (int x = x_beg; x < x_end && ok;) {
-      const Seg sg = seg_at(P, x, x_end);
-      x += sg.kb1 - sg.kb0;
-      const int nk = sg.kb1 - sg.kb0;
-      const int first = (grp - j % kConvGroups + kConvGroups) % kConvGroups;  // this group's first K-block
-      if (first >= nk) {
-        j += nk;
-        continue;
-      }
-      const int u = sg.u;
-      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
-      const int h = u % kG2Slices;
-      const float* sc = a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks;
-      const int kexp = w2_block_exponent(sc);
-      // the unit's 16 scales, one per lane: no global load on the per-stage path
-      const float lane_scale = __ldg(sc + (lane & (kIBlocks - 1)));
-      for (int l = first; l < nk; l += kConvGroups) {
-        const int jj = j + l, kb = sg.kb0 + l;
-        const int rs = jj % SR, cs = jj % SC;
-        if (!mbar_wait(&raw_full[rs], (uint32_t)(jj / SR) & 1u, sAbort, kWaitBudgetNs) ||
-            !mbar_wait(&c_empty[cs], ((uint32_t)(jj / SC) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
-          ok = false;
-          if (lane == 0) fail(kStatusTimeoutConvert);
-          break;
-        }
-        tc_fence_after();  // the MMAs that read this TMEM stage have completed
-        const __half2 sc2 = __half2half2(__float2half_rn(ldexpf(__shfl_sync(0xffffffffu, lane_scale, kb), kexp)));
-        const uint8_t* raw = sRaw + rs * kRawBytes;
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          uint32_t o[32];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 qv = *reinterpret_cast<const uint4*>(raw + sw128_offset(r, 4 * half + i));
-            const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[k] & 0xFFFFu), __NV_E4M3);
-              const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[k] >> 16), __NV_E4M3);
-              const __half2 pl = __hmul2(*reinterpret_cast<const __half2*>(&lo), sc2);
-              const __half2 ph = __hmul2(*reinterpret_cast<const __half2*>(&hi), sc2);
-              o[8 * i + 2 * k] = *reinterpret_cast<const uint32_t*>(&pl);
-              o[8 * i + 2 * k + 1] = *reinterpret_cast<const uint32_t*>(&ph);
-            }
-          }
-          tmem_st32(lane_addr + cs * kA2StageCols + 32 * half, o);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&raw_empty[rs]);
-          mbar_arrive(&a_full[cs]);
-        }
-      }
-      j += nk;
-    }
-  } else if (warp >= 8 && warp < 12) {
-    // ------------------------------------------------------------ epilogue
-    const int ew = warp - 8;
-    const int hrow = ew * 32 + lane;
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ planes + promotion
+    const int set = (warp - 4) >> 2;  // units ug with ug % 4 == set
+    const int ew = warp & 3;          // TMEM lane quarter
+    const int etid = threadIdx.x - 128;
+    const int ewarp = etid >> 5;      // 0..15
+    const int hrow = ew * 32 + lane;  // W2 row of the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    uint32_t ug = 0;
+    uint32_t kgl = 0;
+    int cur_blk = -1, nblk = 0;
+    bool ok = true;
+    int ug = 0;
     for (int x = x_beg; x < x_end; ++ug) {
       const Seg sg = seg_at(P, x, x_end);
       x += sg.kb1 - sg.kb0;
+      const int nk = sg.kb1 - sg.kb0;
       const int u = sg.u;
-      const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
-      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
+      const int b = u / kG2Slices;
+      const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
       const int h = u % kG2Slices;
-      const int r0 = blk.y, nrows = blk.z;
-      const uint32_t buf = ug % kBufs2;
-      if (!mbar_wait(&tfull[buf], (ug / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
-        if (lane == 0) fail(kStatusTimeoutEpilogue);
-        break;
-      }
-      tc_fence_after();
-      __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
-      const float* wrow = a.row_weight + r0;
-      // the converters scaled W2 by 2^k (see w2_block_exponent): undo it exactly
-      const int kexp = w2_block_exponent(a.w2_scale + ((size_t)blk.x * kHBlocks + h) * kIBlocks);
-      bool sat = false;
-      float p[16];
-      tmem_ld16(tmem_base + lane_base + buf * BN, p);
-      tmem_wait_ld();
+      const int e = blk.x, r0 = blk.y, nrows = blk.z;
+      if (b != cur_blk) {
+        // ---- all 16 warps: the new block's two fp8 planes
+        bool bad = !ok;
+        if (etid == 0 && !bad) {
+          // the MMAs on the previous block's planes have completed
+          if (nblk > 0 && !mbar_wait(planes_empty, (uint32_t)(nblk - 1) & 1u, sAbort, kWaitBudgetNs)) {
+            bad = true;
+            fail(kStatusTimeoutEpilogue);
+          }
+          // GEMM1 published all 32 slices of the block's rows
+          const uint64_t t0 = globaltimer_ns();
+          while (!bad && ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
+            if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
+              bad = true;
+              fail(kStatusTimeoutProducer);
+            }
+            __nanosleep(100);
+          }
+        }
+        if (named_barrier_or(2, kEpi2Threads, bad)) break;
+        // warp w builds (token row t, K-block kb) pairs w, w + 16, ...: lanes hold 4 consecutive values
+        for (int task = ewarp; task < BN * kIBlocks; task += kEpi2Threads / 32) {
+          const int t = task / kIBlocks, kb = task % kIBlocks;
+          float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          if (t < nrows) {
+            // L2 reads (.cg): other CTAs wrote these rows; this SM's L1 may hold an older call's
+            const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(a.inter + (size_t)(r0 + t) * kInter + kb * kBlk) +
+                                     lane);
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+            v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+          }
+          float sc[2];
+          uint32_t q[2];
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (i < nrows) dst[(size_t)i * kHidden] = to_half_sat(p[i] * ldexpf(__ldg(wrow + i), -kexp), sat);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
-      if (sat) atomicOr(a.status, kStatusSaturated);
+          for (int pl = 0; pl < 2; ++pl) {
+            float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+            for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+            const float s = m > 0.0f ? __fdiv_rn(m, 448.0f) : 1.0f;
+            uint32_t packed = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float y = fminf(fmaxf(__fdiv_rn(v[i], s), -448.0f), 448.0f);
+              const __nv_fp8_storage_t f8 = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
+              packed |= (uint32_t)f8 << (8 * i);
+              const __half_raw hr = __nv_cvt_fp8_to_halfraw(f8, __NV_E4M3);
+              v[i] = v[i] - __half2float(*reinterpret_cast<const __half*>(&hr)) * s;  // residual for plane 1
+            }
+            q[pl] = packed;
+            sc[pl] = t < nrows ? s : 0.0f;
+          }
+          uint8_t* tile = sPlanes + kb * kPlaneKBytes;
+#pragma unroll
+          for (int pl = 0; pl < 2; ++pl) {
+            const int prow = pl * BN + t;
+            *reinterpret_cast<uint32_t*>(tile + sw128_offset(prow, lane >> 2) + (lane & 3) * 4) = q[pl];
+            if (lane == 0) sPScale[kb * kPlaneRows + prow] = sc[pl];
+          }
+        }
+        fence_proxy_async_smem();  // the planes are read by the tensor core (async proxy)
+        named_barrier_sync(2, kEpi2Threads);
+        if (etid == 0) mbar_arrive(planes_full);
+        ++nblk;
+        cur_blk = b;
+      }
+      if ((ug & 3) == set && ok) {
+        // ---- this set promotes the unit's K-blocks and stores its pair rows
+        const float* sc2 = a.w2_scale + ((size_t)e * kHBlocks + h) * kIBlocks;
+        const float lane_scale = __ldg(sc2 + (lane & (kIBlocks - 1)));
+        float acc[BN];
+#pragma unroll
+        for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
+        for (int l = 0; l < nk; ++l) {
+          const uint32_t kg = kgl + l;
+          const uint32_t buf = kg % kBufs2;
+          if (!mbar_wait(&tfull[buf], (kg / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            if (lane == 0) fail(kStatusTimeoutEpilogue);
+            break;
+          }
+          tc_fence_after();
+          const int kb = sg.kb0 + l;
+          const float ws = __shfl_sync(0xffffffffu, lane_scale, kb);
+          float p0[16], p1[16];
+          tmem_ld16(tmem_base + lane_base + buf * kCols2, p0);
+          tmem_ld16(tmem_base + lane_base + buf * kCols2 + BN, p1);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+          const float* ps = sPScale + kb * kPlaneRows;
+#pragma unroll
+          for (int t = 0; t < BN; ++t) {
+            acc[t] = fmaf(p0[t], ws * ps[t], acc[t]);
+            acc[t] = fmaf(p1[t], ws * ps[BN + t], acc[t]);
+          }
+        }
+        if (ok) {
+          const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
+          __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
+          const float* wrow = a.row_weight + r0;
+          bool sat = false;
+#pragma unroll
+          for (int t = 0; t < BN; ++t)
+            if (t < nrows) dst[(size_t)t * kHidden] = to_half_sat(acc[t] * __ldg(wrow + t), sat);
+          if (sat) atomicOr(a.status, kStatusSaturated);
+        }
+      }
+      kgl += nk;
     }
   }
 }
@@ -910,24 +902,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       mbar_init(&bars1[2 * kStages1 + kBufs1 + b], 4);  // one arrive per warp of the owning set
     }
     mbar_init(&bars1[2 * kStages1 + 2 * kBufs1], 1);
-    // phase 2: raw full/empty, converted full/empty, intermediate full/empty, tfull/tempty, drain
+    // phase 2: raw full/empty, planes full/empty, tfull/tempty, drain
     uint64_t* b2 = bars2;
     for (int s = 0; s < kRawStages; ++s) {
-      mbar_init(&b2[s], 1);
-      mbar_init(&b2[kRawStages + s], 4);  // one arrive per warp of the converting group
+      mbar_init(&b2[s], 1);                // producer's expect_tx arrive
+      mbar_init(&b2[kRawStages + s], 1);   // tcgen05.commit
     }
     b2 += 2 * kRawStages;
-    for (int s = 0; s < kConvStages; ++s) {
-      mbar_init(&b2[s], 4);
-      mbar_init(&b2[kConvStages + s], 1);
-    }
-    b2 += 2 * kConvStages;
-    mbar_init(&b2[0], 1);  // intermediate of a block landed (expect_tx arrive)
-    mbar_init(&b2[1], 1);  // MMA done with it (tcgen05.commit)
+    mbar_init(&b2[0], 1);  // the block's planes written (one arrive)
+    mbar_init(&b2[1], 1);  // MMA done with them (tcgen05.commit)
     b2 += 2;
     for (int b = 0; b < kBufs2; ++b) {
       mbar_init(&b2[b], 1);
-      mbar_init(&b2[kBufs2 + b], 4);
+      mbar_init(&b2[kBufs2 + b], 4);  // one arrive per warp of the promoting set
     }
     mbar_init(&b2[2 * kBufs2], 1);
     *sAbort = 0;
