@@ -109,6 +109,10 @@ constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kPlaneRows = 2 * BN;          // two planes of BN token rows
 constexpr int kPlaneKBytes = kPlaneRows * 128;
 constexpr int kBufs2 = 16;
+// Each set of promotion warps owns kBufsPerSet of the buffers, used in order, so
+// every wait on a buffer's barrier is for the phase right after the one the same
+// waiter last saw (a parity wait cannot alias a phase two completions ahead).
+constexpr int kBufsPerSet = kBufs2 / kSets;
 constexpr int kCols2 = kPlaneRows;          // accumulator columns per buffer
 constexpr int kEpi2Threads = 512;           // warps 4-19
 constexpr int kP2Raw = 0;
@@ -609,14 +613,15 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, kCols2);  // e4m3 x e4m3
       Ring ring(SR);
-      uint32_t kgl = 0;
+      uint32_t cnt[kSets] = {0u, 0u, 0u, 0u};  // K-blocks given to each set so far
       int cur_blk = -1, nblk = 0;
       bool ok = true;
       bool any = false;
-      for (int x = x_beg; x < x_end && ok;) {
+      for (int x = x_beg, ug = 0; x < x_end && ok; ++ug) {
         const Seg sg = seg_at(P, x, x_end);
         x += sg.kb1 - sg.kb0;
         const int b = sg.u / kG2Slices;
+        const int set = ug & (kSets - 1);
         if (b != cur_blk) {
           if (!mbar_wait(planes_full, (uint32_t)nblk & 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
@@ -626,9 +631,10 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           ++nblk;
           cur_blk = b;
         }
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++kgl) {
-          const uint32_t buf = kgl % kBufs2;
-          if (!mbar_wait(&tempty[buf], ((kgl / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+          const uint32_t c = cnt[set]++;
+          const uint32_t buf = kBufsPerSet * set + (c % kBufsPerSet);
+          if (!mbar_wait(&tempty[buf], ((c / kBufsPerSet) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
               !mbar_wait(&raw_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
@@ -663,7 +669,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     const int ewarp = etid >> 5;      // 0..15
     const int hrow = ew * 32 + lane;  // W2 row of the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    uint32_t kgl = 0;
+    uint32_t cnt = 0;  // K-blocks this set promoted so far
     int cur_blk = -1, nblk = 0;
     bool ok = true;
     int ug = 0;
@@ -749,10 +755,9 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         float acc[BN];
 #pragma unroll
         for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
-        for (int l = 0; l < nk; ++l) {
-          const uint32_t kg = kgl + l;
-          const uint32_t buf = kg % kBufs2;
-          if (!mbar_wait(&tfull[buf], (kg / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
+        for (int l = 0; l < nk; ++l, ++cnt) {
+          const uint32_t buf = kBufsPerSet * set + (cnt % kBufsPerSet);
+          if (!mbar_wait(&tfull[buf], (cnt / kBufsPerSet) & 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
             if (lane == 0) fail(kStatusTimeoutEpilogue);
             break;
@@ -785,7 +790,6 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           if (sat) atomicOr(a.status, kStatusSaturated);
         }
       }
-      kgl += nk;
     }
   }
 }
