@@ -613,7 +613,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, kCols2);  // e4m3 x e4m3
       Ring ring(SR);
-      uint32_t cnt[kSets] = {0u, 0u, 0u, 0u};  // K-blocks given to each set so far
+      uint32_t cnt0 = 0, cnt1 = 0, cnt2 = 0, cnt3 = 0;  // K-blocks given to each set so far (registers)
       int cur_blk = -1, nblk = 0;
       bool ok = true;
       bool any = false;
@@ -622,6 +622,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         x += sg.kb1 - sg.kb0;
         const int b = sg.u / kG2Slices;
         const int set = ug & (kSets - 1);
+        uint32_t c = set == 0 ? cnt0 : set == 1 ? cnt1 : set == 2 ? cnt2 : cnt3;
         if (b != cur_blk) {
           if (!mbar_wait(planes_full, (uint32_t)nblk & 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
@@ -631,8 +632,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           ++nblk;
           cur_blk = b;
         }
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
-          const uint32_t c = cnt[set]++;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++c) {
           const uint32_t buf = kBufsPerSet * set + (c % kBufsPerSet);
           if (!mbar_wait(&tempty[buf], ((c / kBufsPerSet) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
               !mbar_wait(&raw_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
@@ -651,6 +651,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           any = true;
           ring.next();
         }
+        if (set == 0) cnt0 = c; else if (set == 1) cnt1 = c; else if (set == 2) cnt2 = c; else cnt3 = c;
         if (!ok) break;
         // another block follows in this CTA's range: release the planes once these MMAs complete
         if (x < x_end && seg_at(P, x, x_end).u / kG2Slices != b) tc_commit(planes_empty);
@@ -702,44 +703,44 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           }
         }
         if (named_barrier_or(2, kEpi2Threads, bad)) break;
-        // warp w builds (token row t, K-block kb) pairs w, w + 16, ...: lanes hold 4 consecutive values
-        for (int task = ewarp; task < BN * kIBlocks; task += kEpi2Threads / 32) {
-          const int t = task / kIBlocks, kb = task % kIBlocks;
-          float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          if (t < nrows) {
-            // L2 reads (.cg): other CTAs wrote these rows; this SM's L1 may hold an older call's
-            const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(a.inter + (size_t)(r0 + t) * kInter + kb * kBlk) +
-                                     lane);
-            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-            v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
-          }
-          float sc[2];
-          uint32_t q[2];
+        // warp w builds K-block kb = w for all 16 token rows; each lane holds 4
+        // consecutive values.  The 16 rows' loads are issued together (one L2 round
+        // trip), then each row is split: scale = amax / 448, q = e4m3(x * 448 / amax).
+        static_assert(kEpi2Threads / 32 == kIBlocks, "one warp per K-block of the intermediate");
+        {
+          const int kb = ewarp;
+          uint2 raw[BN];
 #pragma unroll
-          for (int pl = 0; pl < 2; ++pl) {
-            float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-            for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
-            const float s = m > 0.0f ? __fdiv_rn(m, 448.0f) : 1.0f;
-            uint32_t packed = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float y = fminf(fmaxf(__fdiv_rn(v[i], s), -448.0f), 448.0f);
-              const __nv_fp8_storage_t f8 = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
-              packed |= (uint32_t)f8 << (8 * i);
-              const __half_raw hr = __nv_cvt_fp8_to_halfraw(f8, __NV_E4M3);
-              v[i] = v[i] - __half2float(*reinterpret_cast<const __half*>(&hr)) * s;  // residual for plane 1
-            }
-            q[pl] = packed;
-            sc[pl] = t < nrows ? s : 0.0f;
-          }
+          for (int t = 0; t < BN; ++t)
+            raw[t] = t < nrows ? __ldcg(reinterpret_cast<const uint2*>(a.inter + (size_t)(r0 + t) * kInter +
+                                                                       kb * kBlk) + lane)
+                               : make_uint2(0u, 0u);  // L2 reads: this SM's L1 may hold an older call's rows
           uint8_t* tile = sPlanes + kb * kPlaneKBytes;
+#pragma unroll 4
+          for (int t = 0; t < BN; ++t) {
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw[t].x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw[t].y));
+            float v[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
-          for (int pl = 0; pl < 2; ++pl) {
-            const int prow = pl * BN + t;
-            *reinterpret_cast<uint32_t*>(tile + sw128_offset(prow, lane >> 2) + (lane & 3) * 4) = q[pl];
-            if (lane == 0) sPScale[kb * kPlaneRows + prow] = sc[pl];
+            for (int pl = 0; pl < 2; ++pl) {
+              float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+              for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+              const float sc = m > 0.0f ? m * (1.0f / 448.0f) : 1.0f;
+              const float inv = m > 0.0f ? __fdividef(448.0f, m) : 1.0f;
+              uint32_t packed = 0;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float y = fminf(fmaxf(v[i] * inv, -448.0f), 448.0f);
+                const __nv_fp8_storage_t f8 = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
+                packed |= (uint32_t)f8 << (8 * i);
+                const __half_raw hr = __nv_cvt_fp8_to_halfraw(f8, __NV_E4M3);
+                v[i] = v[i] - __half2float(*reinterpret_cast<const __half*>(&hr)) * sc;  // residual for plane 1
+              }
+              const int prow = pl * BN + t;
+              *reinterpret_cast<uint32_t*>(tile + sw128_offset(prow, lane >> 2) + (lane & 3) * 4) = packed;
+              if (lane == 0) sPScale[kb * kPlaneRows + prow] = t < nrows ? sc : 0.0f;
+            }
           }
         }
         fence_proxy_async_smem();  // the planes are read by the tensor core (async proxy)
