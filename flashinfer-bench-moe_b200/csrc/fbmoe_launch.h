@@ -87,6 +87,7 @@ struct Layout {
   size_t blk_ready;    // int32[max_blocks]: GEMM1 slices published per block (decode kernel)
   size_t grid_sync;    // int32[1]: CTAs of the decode kernel done with GEMM2 (zeroed by permute)
   size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
+  size_t plane_scale;  // fp32[2][pcap][32]  scales of the decode kernel's fp8 intermediate planes (16-row blocks only)
   size_t total;        // bytes
   int tokens;          // T the layout was made for
   int pcap;            // row capacity (multiple of 128)
@@ -139,7 +140,8 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
 // per-token combine in one persistent kernel; writes out (bf16, or fp32 partial
 // sums with f32_out).
 // sink: host-visible status sink of the workspace (nullptr: none).
-cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_planes,
+                          const CUtensorMap* tm_pscale,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
                           uint32_t* sink, bool w1_packed, cudaStream_t stream);

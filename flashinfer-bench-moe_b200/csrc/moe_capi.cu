@@ -76,6 +76,7 @@ Layout make_layout(int T, int E_local, bool allow_split, int force_rows) {
   L.chunk_cnt = take((tt + 1023) / 1024 * (size_t)el * 4);
   L.a_perm = take(big ? (size_t)pcap * kHidden : 0);
   L.a_scale_perm = take(big ? (size_t)pcap * kHBlocks * 4 : 0);
+  L.plane_scale = take(bn == 16 ? (size_t)2 * pcap * (kInter / 64) * 4 : 0);
   L.e_local = el;
   L.total = off;
   return L;
@@ -258,9 +259,21 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   rc = encode_2d(&tm_w2raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 64,
                  256, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
-                 (uint32_t)bn);
-  if (rc) return rc;
+  CUtensorMap tm_planes, tm_pscale;
+  if (bn == 16) {
+    // decode: GEMM1 writes the intermediate as two fp8 planes [2][pcap][2048] (in the
+    // f16 intermediate's region) with scales [2][pcap][32]; GEMM2 loads 16-row boxes
+    rc = encode_2d(&tm_planes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + L.inter, kInter, 2 * (uint64_t)L.pcap, 128,
+                   16);
+    if (rc) return rc;
+    rc = encode_2d(&tm_pscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.plane_scale, kInter / 64,
+                   2 * (uint64_t)L.pcap, kInter / 64, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
+                   (uint32_t)bn);
+    if (rc) return rc;
+  }
 
   int fwd = -1;
   if (g_prof.on) {
@@ -292,7 +305,8 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   if (bn == 16) {
     // decode: GEMM1, GEMM2 and the combine run as one kernel (its time is the
     // "gemm1" stage of the profile; "gemm2" and "combine" stay empty)
-    e = launch_decode(&tm_w1, &tm_w2, &tm_inter, reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale,
+    e = launch_decode(&tm_w1, &tm_w2, &tm_planes, &tm_pscale, reinterpret_cast<const uint8_t*>(hidden_states),
+                      hidden_states_scale,
                       T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, sink, w1_packed,
                       stream);
     if (e != cudaSuccess) return from_cuda(e);

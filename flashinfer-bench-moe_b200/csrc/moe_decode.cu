@@ -114,11 +114,11 @@ constexpr int kBufs2 = 16;
 // waiter last saw (a parity wait cannot alias a phase two completions ahead).
 constexpr int kBufsPerSet = kBufs2 / kSets;
 constexpr int kCols2 = kPlaneRows;          // accumulator columns per buffer
-constexpr int kEpi2Threads = 512;           // warps 4-19
+constexpr int kChunks = kInter / 64;         // 64-column chunks of the intermediate (plane scale blocks)
 constexpr int kP2Raw = 0;
 constexpr int kP2Planes = kP2Raw + kRawStages * kRawBytes;
 constexpr int kP2PScale = kP2Planes + kIBlocks * kPlaneKBytes;
-constexpr int kP2End = kP2PScale + kIBlocks * kPlaneRows * 4;
+constexpr int kP2End = kP2PScale + 2 * BN * kChunks * 4;
 constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
 // ---- barriers and flags (not reused across phases)
 constexpr int kNumBars1 = 2 * kStages1 + 2 * kBufs1 + 1;
@@ -136,7 +136,8 @@ static_assert(kP2Planes % 1024 == 0, "the planes are 128-byte swizzle atoms");
 struct DecodeArgs {
   CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
   CUtensorMap tm_w2;     // W2 rows x 2048 K, 128-byte x 128-row boxes
-  CUtensorMap tm_inter;  // inter rows x 2048 f16, 64-column x 16-row boxes
+  CUtensorMap tm_planes;  // GEMM2 B planes: [2 * pcap rows] x 2048 fp8, 128-byte x 16-row boxes
+  CUtensorMap tm_pscale;  // their scales: [2 * pcap rows] x 32 fp32, 32 x 16 boxes
   const uint8_t* hidden;
   const float* hidden_scale;
   const float* w1_scale;
@@ -151,7 +152,8 @@ struct DecodeArgs {
   float* split_part;
   int32_t* blk_ready;
   int32_t* grid_sync;
-  __half* inter;
+  uint8_t* planes;         // [2][pcap][2048] fp8: the intermediate as two planes (GEMM1 -> GEMM2)
+  float* plane_scale;      // [2][pcap][32] fp32: their per-(row, 64-column chunk) scales
   __half* pair_out;
   void* out;
   uint32_t* status;
@@ -497,29 +499,60 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         if (last) __threadfence();
       }
       if (last) {
-        // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).
+        // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).  Warp
+        // w takes token row t = w, lane l its columns 2l and 2l + 1 of the slice.  The
+        // row's 64 values are stored as two fp8 planes with one scale each (GEMM2's B
+        // operand, see gemm2_phase): s0 = amax / 448, q0 = e4m3(y * 448 / amax), then
+        // the same for the residual y - q0 * s0.
         const int c0 = P.first_owner(u);
-        for (int i = etid; i < 64 * BN; i += kEpi1Threads) {
-          const int r = i % 64, t = i / 64;
-          if (t < nrows) {
+        const int t = etid >> 5;  // 16 warps, 16 token rows
+        const int r = 2 * lane;
+        float y[2] = {0.0f, 0.0f};
+        if (t < nrows) {
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
             float x1 = 0.0f, x2 = 0.0f;
             if (nseg == 1) {
 #pragma unroll
               for (int j = 0; j < G; ++j) {
-                x1 += sXch[(size_t)(j * 128 + r) * kXchStride + t];
-                x2 += sXch[(size_t)(j * 128 + 64 + r) * kXchStride + t];
+                x1 += sXch[(size_t)(j * 128 + r + cc) * kXchStride + t];
+                x2 += sXch[(size_t)(j * 128 + 64 + r + cc) * kXchStride + t];
               }
             } else {
               for (int q = 0; q < nseg; ++q) {  // segment order: deterministic
                 const float* pq = a.split_part + (size_t)partial_slot(P, c0 + q, u) * 128 * BN;
-                x1 += __ldcg(pq + r * BN + t);
-                x2 += __ldcg(pq + (64 + r) * BN + t);
+                x1 += __ldcg(pq + (r + cc) * BN + t);
+                x2 += __ldcg(pq + (64 + r + cc) * BN + t);
               }
             }
-            bool sat = false;
-            const float silu = x2 / (1.0f + expf(-x2));
-            a.inter[(size_t)(r0 + t) * kInter + 64 * g + r] = to_half_sat(silu * x1, sat);
-            if (sat) atomicOr(a.status, kStatusSaturated);
+            y[cc] = x2 / (1.0f + expf(-x2)) * x1;
+          }
+        }
+        if (!isfinite(y[0]) || !isfinite(y[1])) {
+          atomicOr(a.status, kStatusSaturated);
+          y[0] = isfinite(y[0]) ? y[0] : 0.0f;
+          y[1] = isfinite(y[1]) ? y[1] : 0.0f;
+        }
+#pragma unroll
+        for (int pl = 0; pl < 2; ++pl) {
+          float m = fmaxf(fabsf(y[0]), fabsf(y[1]));
+#pragma unroll
+          for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+          const float sc = m > 0.0f ? m * (1.0f / 448.0f) : 1.0f;
+          const float inv = m > 0.0f ? __fdividef(448.0f, m) : 1.0f;
+          uint32_t packed = 0;
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const float v = fminf(fmaxf(y[cc] * inv, -448.0f), 448.0f);
+            const __nv_fp8_storage_t f8 = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+            packed |= (uint32_t)f8 << (8 * cc);
+            const __half_raw hr = __nv_cvt_fp8_to_halfraw(f8, __NV_E4M3);
+            y[cc] -= __half2float(*reinterpret_cast<const __half*>(&hr)) * sc;  // residual for plane 1
+          }
+          if (t < nrows) {
+            const size_t prow = (size_t)pl * a.pcap + r0 + t;
+            *reinterpret_cast<uint16_t*>(a.planes + prow * kInter + 64 * g + r) = (uint16_t)packed;
+            if (lane == 0) a.plane_scale[prow * kChunks + g] = sc;
           }
         }
         if (nseg > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
@@ -533,37 +566,34 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 }
 
 // ============================================================== GEMM2 phase
-// The intermediate of a block (<= 16 token rows x 2048, f16 from GEMM1) is
-// split into two fp8 planes with their own scales per (token row, 128-K block):
-//     s0 = amax|x| / 448,  q0 = e4m3(x / s0),  r = x - q0 * s0,
-//     s1 = amax|r| / 448,  q1 = e4m3(r / s1),  x ~ q0 * s0 + q1 * s1
-// (the same 1x128 rule as the activations, applied twice).  GEMM2 then runs as
-// kind::f8f6f4 straight on the fp8 W2 tile, with no dequantisation of W2: per
-// K-block one MMA chain of N = 32 (both planes) into a TMEM buffer, promoted by
+// GEMM1 stored each block's intermediate as two fp8 planes, per (token row,
+// 64-column chunk) with its own scale (q0 * s0 + q1 * s1 ~ the fp32 SwiGLU output,
+// the 1x64 block rule applied to the value and then to its residual).  GEMM2 runs
+// as kind::f8f6f4 straight on the fp8 W2 tile -- no dequantisation of W2 -- with
+// the two planes stacked as the N = 32 operand, and is promoted per 64-K chunk by
 // the W2 block scale times each plane's scale:
-//     acc[t] += s2[h, kb] * (s0[t, kb] * D[:, t] + s1[t, kb] * D[:, 16 + t])
-// W2 itself enters exactly (fp8 times its fp32 scale), and two planes keep about
-// eight significant bits of every intermediate value relative to its block's
-// largest; measured on the host against the fp32 intermediate, the worst pair-row
-// element is within 0.13x the output tolerance, against 0.08x for the f16
-// intermediate with f16 W2 this replaces (and 0.40x for bf16, 5.8x for one fp8
-// plane).
+//     acc[t] += s2[h, kb] * (s0[t, c] * D[:, t] + s1[t, c] * D[:, 16 + t])
+// W2 enters exactly (fp8 times its fp32 scale); two planes keep about eight
+// significant bits of every intermediate value relative to its chunk's largest.
+// Measured on the host against the fp32 intermediate, the worst pair-row element is
+// within 0.13x the output tolerance (0.08x for the f16 intermediate with f16 W2 this
+// replaces, 0.40x for bf16, 5.8x for a single fp8 plane).
 //
-// Warps: w0 W2 producer (TMA ring), w1 MMA issuer, w4-w19 build the planes of
-// each new block together (after the block's 32 GEMM1 slices are published and
-// the MMAs on the previous block's planes have completed), then promote: a unit's
+// Warps: w0 W2 producer (TMA ring); w2 loads a block's planes and scales (TMA,
+// once per block, after GEMM1 published the block's 32 slices and the MMAs on the
+// previous block's planes completed); w1 MMA issuer; w4-w19 promote: a unit's
 // K-blocks are promoted by one set of four warps (units go to the sets round
-// robin), which at the unit's end multiplies by the routing weight and stores the
-// f16 pair rows of its segment's plane.
+// robin, each set owning four TMEM buffers), which at the unit's end multiplies by
+// the routing weight and stores the f16 pair rows of its segment's plane.
 __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
                                             int nb, volatile int* sAbort) {
   constexpr int SR = kRawStages;
   uint8_t* sRaw = sm + kP2Raw;
   uint8_t* sPlanes = sm + kP2Planes;
-  float* sPScale = reinterpret_cast<float*>(sm + kP2PScale);  // [16 K-blocks][32 plane rows]
+  const float* sPScale = reinterpret_cast<const float*>(sm + kP2PScale);  // [2 planes][16 rows][32 chunks]
   uint64_t* raw_full = bars;                  // W2 tile landed (TMA)
   uint64_t* raw_empty = bars + SR;            // MMA done with it (tcgen05.commit)
-  uint64_t* planes_full = bars + 2 * SR;      // the block's planes are written (one arrive)
+  uint64_t* planes_full = bars + 2 * SR;      // a block's planes and scales landed (TMA)
   uint64_t* planes_empty = planes_full + 1;   // MMA done with them (another block follows)
   uint64_t* tfull = planes_full + 2;
   uint64_t* tempty = tfull + kBufs2;
@@ -608,12 +638,57 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           if (!mbar_wait_drain(&raw_full[s], last_parity[s], kWaitBudgetNs)) fail(kStatusTimeoutDrain);
     }
     __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ planes producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();
+      int cur_blk = -1, nblk = 0;
+      bool ok = true;
+      for (int x = x_beg; x < x_end && ok;) {
+        const Seg sg = seg_at(P, x, x_end);
+        x += sg.kb1 - sg.kb0;
+        const int b = sg.u / kG2Slices;
+        if (b == cur_blk) continue;
+        // the MMAs on the previous block's planes have completed
+        if (nblk > 0 && !mbar_wait(planes_empty, (uint32_t)(nblk - 1) & 1u, sAbort, kWaitBudgetNs)) {
+          fail(kStatusTimeoutProducer);
+          break;
+        }
+        // GEMM1 published all 32 slices of the block's rows
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
+          if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
+            ok = false;
+            fail(kStatusTimeoutProducer);
+            break;
+          }
+          __nanosleep(100);
+        }
+        if (!ok) break;
+        fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
+        const int r0 = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status).y;
+        mbar_arrive_expect_tx(planes_full, kIBlocks * kPlaneKBytes + 2 * BN * kChunks * 4);
+        for (int kb = 0; kb < kIBlocks; ++kb)
+#pragma unroll
+          for (int pl = 0; pl < 2; ++pl)
+            tma_load_2d(sPlanes + kb * kPlaneKBytes + pl * BN * 128, &a.tm_planes, planes_full, kb * kBlk,
+                        pl * a.pcap + r0, pol);
+#pragma unroll
+        for (int pl = 0; pl < 2; ++pl)
+          tma_load_2d(sm + kP2PScale + pl * BN * kChunks * 4, &a.tm_pscale, planes_full, 0, pl * a.pcap + r0, pol);
+        ++nblk;
+        cur_blk = b;
+      }
+      if (nblk > 0 && !mbar_wait_drain(planes_full, (uint32_t)(nblk - 1) & 1u, kWaitBudgetNs))
+        fail(kStatusTimeoutDrain);
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, kCols2);  // e4m3 x e4m3
       Ring ring(SR);
-      uint32_t cnt0 = 0, cnt1 = 0, cnt2 = 0, cnt3 = 0;  // K-blocks given to each set so far (registers)
+      uint32_t cnt0 = 0, cnt1 = 0, cnt2 = 0, cnt3 = 0;  // buffer uses given to each set so far
       int cur_blk = -1, nblk = 0;
       bool ok = true;
       bool any = false;
@@ -632,22 +707,31 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           ++nblk;
           cur_blk = b;
         }
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++c) {
-          const uint32_t buf = kBufsPerSet * set + (c % kBufsPerSet);
-          if (!mbar_wait(&tempty[buf], ((c / kBufsPerSet) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
-              !mbar_wait(&raw_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
+        for (int kb = sg.kb0; kb < sg.kb1 && ok; ++kb) {
+          if (!mbar_wait(&raw_full[ring.slot], ring.phase, sAbort, kWaitBudgetNs)) {
             ok = false;
             fail(kStatusTimeoutMma);
             break;
           }
-          tc_fence_after();
           const uint64_t adesc = umma_desc_sw128(smem_u32(sRaw + ring.slot * kRawBytes));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(sPlanes + kb * kPlaneKBytes));
-          const uint32_t d = tmem_base + buf * kCols2;
+          // two 64-K chunks, each into its own buffer (promoted with its own plane scales)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) mma_f8f6f4(d, adesc + 2 * j, bdesc + 2 * j, idesc, j > 0 ? 1u : 0u);
+          for (int ch = 0; ch < 2; ++ch, ++c) {
+            const uint32_t buf = kBufsPerSet * set + (c % kBufsPerSet);
+            if (!mbar_wait(&tempty[buf], ((c / kBufsPerSet) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
+              ok = false;
+              fail(kStatusTimeoutMma);
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem_base + buf * kCols2;
+            mma_f8f6f4(d, adesc + 4 * ch, bdesc + 4 * ch, idesc, 0u);
+            mma_f8f6f4(d, adesc + 4 * ch + 2, bdesc + 4 * ch + 2, idesc, 1u);
+            tc_commit(&tfull[buf]);
+          }
+          if (!ok) break;
           tc_commit(&raw_empty[ring.slot]);
-          tc_commit(&tfull[buf]);
           any = true;
           ring.next();
         }
@@ -663,134 +747,61 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     }
     __syncwarp();
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ planes + promotion
+    // ------------------------------------------------------------ promotion
     const int set = (warp - 4) >> 2;  // units ug with ug % 4 == set
     const int ew = warp & 3;          // TMEM lane quarter
-    const int etid = threadIdx.x - 128;
-    const int ewarp = etid >> 5;      // 0..15
     const int hrow = ew * 32 + lane;  // W2 row of the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    uint32_t cnt = 0;  // K-blocks this set promoted so far
-    int cur_blk = -1, nblk = 0;
+    uint32_t cnt = 0;  // buffer uses of this set so far
     bool ok = true;
     int ug = 0;
-    for (int x = x_beg; x < x_end; ++ug) {
+    for (int x = x_beg; x < x_end && ok; ++ug) {
       const Seg sg = seg_at(P, x, x_end);
       x += sg.kb1 - sg.kb0;
       const int nk = sg.kb1 - sg.kb0;
+      if ((ug & (kSets - 1)) != set) continue;
       const int u = sg.u;
-      const int b = u / kG2Slices;
-      const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
+      const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
       const int h = u % kG2Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
-      if (b != cur_blk) {
-        // ---- all 16 warps: the new block's two fp8 planes
-        bool bad = !ok;
-        if (etid == 0 && !bad) {
-          // the MMAs on the previous block's planes have completed
-          if (nblk > 0 && !mbar_wait(planes_empty, (uint32_t)(nblk - 1) & 1u, sAbort, kWaitBudgetNs)) {
-            bad = true;
-            fail(kStatusTimeoutEpilogue);
-          }
-          // GEMM1 published all 32 slices of the block's rows
-          const uint64_t t0 = globaltimer_ns();
-          while (!bad && ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
-            if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
-              bad = true;
-              fail(kStatusTimeoutProducer);
-            }
-            __nanosleep(100);
-          }
+      const float lane_scale = __ldg(a.w2_scale + ((size_t)e * kHBlocks + h) * kIBlocks + (lane & (kIBlocks - 1)));
+      float acc[BN];
+#pragma unroll
+      for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
+      for (int l = 0; l < 2 * nk; ++l, ++cnt) {
+        const uint32_t buf = kBufsPerSet * set + (cnt % kBufsPerSet);
+        if (!mbar_wait(&tfull[buf], (cnt / kBufsPerSet) & 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutEpilogue);
+          break;
         }
-        if (named_barrier_or(2, kEpi2Threads, bad)) break;
-        // warp w builds K-block kb = w for all 16 token rows; each lane holds 4
-        // consecutive values.  The 16 rows' loads are issued together (one L2 round
-        // trip), then each row is split: scale = amax / 448, q = e4m3(x * 448 / amax).
-        static_assert(kEpi2Threads / 32 == kIBlocks, "one warp per K-block of the intermediate");
-        {
-          const int kb = ewarp;
-          uint2 raw[BN];
+        tc_fence_after();
+        const int chunk = 2 * sg.kb0 + l;  // 64-K chunk of the intermediate
+        const float ws = __shfl_sync(0xffffffffu, lane_scale, chunk >> 1);
+        float p0[16], p1[16];
+        tmem_ld16(tmem_base + lane_base + buf * kCols2, p0);
+        tmem_ld16(tmem_base + lane_base + buf * kCols2 + BN, p1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        const float* s0 = sPScale + chunk;             // plane 0, row t: s0[t * kChunks]
+        const float* s1 = sPScale + BN * kChunks + chunk;
 #pragma unroll
-          for (int t = 0; t < BN; ++t)
-            raw[t] = t < nrows ? __ldcg(reinterpret_cast<const uint2*>(a.inter + (size_t)(r0 + t) * kInter +
-                                                                       kb * kBlk) + lane)
-                               : make_uint2(0u, 0u);  // L2 reads: this SM's L1 may hold an older call's rows
-          uint8_t* tile = sPlanes + kb * kPlaneKBytes;
-#pragma unroll 4
-          for (int t = 0; t < BN; ++t) {
-            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw[t].x));
-            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw[t].y));
-            float v[4] = {lo.x, lo.y, hi.x, hi.y};
-#pragma unroll
-            for (int pl = 0; pl < 2; ++pl) {
-              float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-              for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
-              const float sc = m > 0.0f ? m * (1.0f / 448.0f) : 1.0f;
-              const float inv = m > 0.0f ? __fdividef(448.0f, m) : 1.0f;
-              uint32_t packed = 0;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float y = fminf(fmaxf(v[i] * inv, -448.0f), 448.0f);
-                const __nv_fp8_storage_t f8 = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
-                packed |= (uint32_t)f8 << (8 * i);
-                const __half_raw hr = __nv_cvt_fp8_to_halfraw(f8, __NV_E4M3);
-                v[i] = v[i] - __half2float(*reinterpret_cast<const __half*>(&hr)) * sc;  // residual for plane 1
-              }
-              const int prow = pl * BN + t;
-              *reinterpret_cast<uint32_t*>(tile + sw128_offset(prow, lane >> 2) + (lane & 3) * 4) = packed;
-              if (lane == 0) sPScale[kb * kPlaneRows + prow] = t < nrows ? sc : 0.0f;
-            }
-          }
-        }
-        fence_proxy_async_smem();  // the planes are read by the tensor core (async proxy)
-        named_barrier_sync(2, kEpi2Threads);
-        if (etid == 0) mbar_arrive(planes_full);
-        ++nblk;
-        cur_blk = b;
-      }
-      if ((ug & 3) == set && ok) {
-        // ---- this set promotes the unit's K-blocks and stores its pair rows
-        const float* sc2 = a.w2_scale + ((size_t)e * kHBlocks + h) * kIBlocks;
-        const float lane_scale = __ldg(sc2 + (lane & (kIBlocks - 1)));
-        float acc[BN];
-#pragma unroll
-        for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
-        for (int l = 0; l < nk; ++l, ++cnt) {
-          const uint32_t buf = kBufsPerSet * set + (cnt % kBufsPerSet);
-          if (!mbar_wait(&tfull[buf], (cnt / kBufsPerSet) & 1u, sAbort, kWaitBudgetNs)) {
-            ok = false;
-            if (lane == 0) fail(kStatusTimeoutEpilogue);
-            break;
-          }
-          tc_fence_after();
-          const int kb = sg.kb0 + l;
-          const float ws = __shfl_sync(0xffffffffu, lane_scale, kb);
-          float p0[16], p1[16];
-          tmem_ld16(tmem_base + lane_base + buf * kCols2, p0);
-          tmem_ld16(tmem_base + lane_base + buf * kCols2 + BN, p1);
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
-          const float* ps = sPScale + kb * kPlaneRows;
-#pragma unroll
-          for (int t = 0; t < BN; ++t) {
-            acc[t] = fmaf(p0[t], ws * ps[t], acc[t]);
-            acc[t] = fmaf(p1[t], ws * ps[BN + t], acc[t]);
-          }
-        }
-        if (ok) {
-          const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
-          __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
-          const float* wrow = a.row_weight + r0;
-          bool sat = false;
-#pragma unroll
-          for (int t = 0; t < BN; ++t)
-            if (t < nrows) dst[(size_t)t * kHidden] = to_half_sat(acc[t] * __ldg(wrow + t), sat);
-          if (sat) atomicOr(a.status, kStatusSaturated);
+        for (int t = 0; t < BN; ++t) {
+          acc[t] = fmaf(p0[t], ws * s0[t * kChunks], acc[t]);
+          acc[t] = fmaf(p1[t], ws * s1[t * kChunks], acc[t]);
         }
       }
+      if (!ok) break;
+      const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
+      __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
+      const float* wrow = a.row_weight + r0;
+      bool sat = false;
+#pragma unroll
+      for (int t = 0; t < BN; ++t)
+        if (t < nrows) dst[(size_t)t * kHidden] = to_half_sat(acc[t] * __ldg(wrow + t), sat);
+      if (sat) atomicOr(a.status, kStatusSaturated);
     }
   }
 }
@@ -928,7 +939,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&a.tm_w1);
     tma_prefetch_desc(&a.tm_w2);
-    tma_prefetch_desc(&a.tm_inter);
+    tma_prefetch_desc(&a.tm_planes);
+    tma_prefetch_desc(&a.tm_pscale);
   }
   if (warp == 1) {
     tmem_alloc(sTmem, kTmemCols);
@@ -981,7 +993,8 @@ static std::atomic<int> g_decode_mode{0};
 
 int decode_launch_mode() { return g_decode_mode.load(std::memory_order_relaxed); }
 
-cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_inter,
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_planes,
+                          const CUtensorMap* tm_pscale,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
                           uint32_t* sink, bool w1_packed, cudaStream_t stream) {
@@ -990,7 +1003,8 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   DecodeArgs a;
   a.tm_w1 = *tm_w1;
   a.tm_w2 = *tm_w2;
-  a.tm_inter = *tm_inter;
+  a.tm_planes = *tm_planes;
+  a.tm_pscale = *tm_pscale;
   a.hidden = hidden;
   a.hidden_scale = hidden_scale;
   a.w1_scale = w1_scale;
@@ -1005,7 +1019,8 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.split_part = reinterpret_cast<float*>(ws + L.split_part);
   a.blk_ready = reinterpret_cast<int32_t*>(ws + L.blk_ready);
   a.grid_sync = reinterpret_cast<int32_t*>(ws + L.grid_sync);
-  a.inter = reinterpret_cast<__half*>(ws + L.inter);
+  a.planes = ws + L.inter;  // the f16 intermediate's region holds the two fp8 planes
+  a.plane_scale = reinterpret_cast<float*>(ws + L.plane_scale);
   a.pair_out = reinterpret_cast<__half*>(ws + L.pair_out);
   a.out = out;
   a.status = reinterpret_cast<uint32_t*>(ws + L.status);
