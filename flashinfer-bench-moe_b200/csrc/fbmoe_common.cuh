@@ -416,6 +416,16 @@ __device__ __forceinline__ void f32x2_fma(uint64_t& acc, uint64_t x, uint64_t y)
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(x), "l"(y));
 }
 
+// Warp-collective TMEM load: 32 lanes x 4 consecutive fp32 columns.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Warp-collective TMEM load of 32 consecutive fp32 columns as 16 packed pairs.
 __device__ __forceinline__ void tmem_ld32_pairs(uint32_t taddr, uint64_t (&v)[16]) {
   uint32_t r[32];

@@ -87,7 +87,7 @@ struct Layout {
   size_t blk_ready;    // int32[max_blocks]: GEMM1 slices published per block (decode kernel)
   size_t grid_sync;    // int32[1]: CTAs of the decode kernel done with GEMM2 (zeroed by permute)
   size_t a_scale_perm;  // fp32[56 * pcap]    their 1x128 scales, [K-block][row] (128-row blocks only)
-  size_t plane_scale;  // fp32[2][pcap][32]  scales of the decode kernel's fp8 intermediate planes (16-row blocks only)
+  size_t plane_scale;  // fp32[2][32][pcap]  scales of the decode kernel's fp8 intermediate planes (16-row blocks only)
   size_t total;        // bytes
   int tokens;          // T the layout was made for
   int pcap;            // row capacity (multiple of 128)

@@ -262,12 +262,12 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   CUtensorMap tm_planes, tm_pscale;
   if (bn == 16) {
     // decode: GEMM1 writes the intermediate as two fp8 planes [2][pcap][2048] (in the
-    // f16 intermediate's region) with scales [2][pcap][32]; GEMM2 loads 16-row boxes
+    // f16 intermediate's region) with scales [2][32][pcap]; GEMM2 loads a block's 16 rows
     rc = encode_2d(&tm_planes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + L.inter, kInter, 2 * (uint64_t)L.pcap, 128,
                    16);
     if (rc) return rc;
-    rc = encode_2d(&tm_pscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.plane_scale, kInter / 64,
-                   2 * (uint64_t)L.pcap, kInter / 64, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = encode_2d(&tm_pscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.plane_scale, (uint64_t)L.pcap,
+                   2 * (kInter / 64), 16, kInter / 64, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   } else {
     rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,

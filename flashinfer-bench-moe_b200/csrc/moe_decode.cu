@@ -59,6 +59,8 @@
 // Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 intermediate producer (TMA),
 // w4-w7, w12-w15 and w16-w19 converter groups, w8-w11 epilogue, w3 idle; then all
 // threads combine.
+#include <cstdlib>
+
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
 
@@ -109,10 +111,9 @@ constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kPlaneRows = 2 * BN;          // two planes of BN token rows
 constexpr int kPlaneKBytes = kPlaneRows * 128;
 constexpr int kBufs2 = 16;
-// Each set of promotion warps owns kBufsPerSet of the buffers, used in order, so
-// every wait on a buffer's barrier is for the phase right after the one the same
-// waiter last saw (a parity wait cannot alias a phase two completions ahead).
-constexpr int kBufsPerSet = kBufs2 / kSets;
+// Every promotion warp waits on every buffer use in order, so each parity wait is
+// for the phase right after the one the same waiter last saw (a parity wait cannot
+// alias a phase two completions ahead).
 constexpr int kCols2 = kPlaneRows;          // accumulator columns per buffer
 constexpr int kChunks = kInter / 64;         // 64-column chunks of the intermediate (plane scale blocks)
 constexpr int kP2Raw = 0;
@@ -137,7 +138,7 @@ struct DecodeArgs {
   CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
   CUtensorMap tm_w2;     // W2 rows x 2048 K, 128-byte x 128-row boxes
   CUtensorMap tm_planes;  // GEMM2 B planes: [2 * pcap rows] x 2048 fp8, 128-byte x 16-row boxes
-  CUtensorMap tm_pscale;  // their scales: [2 * pcap rows] x 32 fp32, 32 x 16 boxes
+  CUtensorMap tm_pscale;  // their scales: [2 * 32 chunk rows] x pcap fp32, 16 x 32 boxes
   const uint8_t* hidden;
   const float* hidden_scale;
   const float* w1_scale;
@@ -153,7 +154,7 @@ struct DecodeArgs {
   int32_t* blk_ready;
   int32_t* grid_sync;
   uint8_t* planes;         // [2][pcap][2048] fp8: the intermediate as two planes (GEMM1 -> GEMM2)
-  float* plane_scale;      // [2][pcap][32] fp32: their per-(row, 64-column chunk) scales
+  float* plane_scale;      // [2][32][pcap] fp32: their per-(64-column chunk, row) scales
   __half* pair_out;
   void* out;
   uint32_t* status;
@@ -552,7 +553,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
           if (t < nrows) {
             const size_t prow = (size_t)pl * a.pcap + r0 + t;
             *reinterpret_cast<uint16_t*>(a.planes + prow * kInter + 64 * g + r) = (uint16_t)packed;
-            if (lane == 0) a.plane_scale[prow * kChunks + g] = sc;
+            if (lane == 0) a.plane_scale[((size_t)pl * kChunks + g) * a.pcap + r0 + t] = sc;
           }
         }
         if (nseg > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
@@ -581,16 +582,15 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 //
 // Warps: w0 W2 producer (TMA ring); w2 loads a block's planes and scales (TMA,
 // once per block, after GEMM1 published the block's 32 slices and the MMAs on the
-// previous block's planes completed); w1 MMA issuer; w4-w19 promote: a unit's
-// K-blocks are promoted by one set of four warps (units go to the sets round
-// robin, each set owning four TMEM buffers), which at the unit's end multiplies by
-// the routing weight and stores the f16 pair rows of its segment's plane.
+// previous block's planes completed); w1 MMA issuer; w4-w19 promote every chunk,
+// each warp four token rows of its TMEM lane quarter, and at a unit's end multiply
+// by the routing weights and store the f16 pair rows of the segment's plane.
 __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, uint64_t* bars, uint32_t tmem_base,
                                             int nb, volatile int* sAbort) {
   constexpr int SR = kRawStages;
   uint8_t* sRaw = sm + kP2Raw;
   uint8_t* sPlanes = sm + kP2Planes;
-  const float* sPScale = reinterpret_cast<const float*>(sm + kP2PScale);  // [2 planes][16 rows][32 chunks]
+  const float* sPScale = reinterpret_cast<const float*>(sm + kP2PScale);  // [2 planes][32 chunks][16 rows]
   uint64_t* raw_full = bars;                  // W2 tile landed (TMA)
   uint64_t* raw_empty = bars + SR;            // MMA done with it (tcgen05.commit)
   uint64_t* planes_full = bars + 2 * SR;      // a block's planes and scales landed (TMA)
@@ -675,7 +675,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
                         pl * a.pcap + r0, pol);
 #pragma unroll
         for (int pl = 0; pl < 2; ++pl)
-          tma_load_2d(sm + kP2PScale + pl * BN * kChunks * 4, &a.tm_pscale, planes_full, 0, pl * a.pcap + r0, pol);
+          tma_load_2d(sm + kP2PScale + pl * BN * kChunks * 4, &a.tm_pscale, planes_full, r0, pl * kChunks, pol);
         ++nblk;
         cur_blk = b;
       }
@@ -688,7 +688,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, kCols2);  // e4m3 x e4m3
       Ring ring(SR);
-      uint32_t cnt0 = 0, cnt1 = 0, cnt2 = 0, cnt3 = 0;  // buffer uses given to each set so far
+      uint32_t c = 0;  // buffer uses so far (two per K-block)
       int cur_blk = -1, nblk = 0;
       bool ok = true;
       bool any = false;
@@ -696,8 +696,6 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         const Seg sg = seg_at(P, x, x_end);
         x += sg.kb1 - sg.kb0;
         const int b = sg.u / kG2Slices;
-        const int set = ug & (kSets - 1);
-        uint32_t c = set == 0 ? cnt0 : set == 1 ? cnt1 : set == 2 ? cnt2 : cnt3;
         if (b != cur_blk) {
           if (!mbar_wait(planes_full, (uint32_t)nblk & 1u, sAbort, kWaitBudgetNs)) {
             ok = false;
@@ -718,8 +716,8 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           // two 64-K chunks, each into its own buffer (promoted with its own plane scales)
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch, ++c) {
-            const uint32_t buf = kBufsPerSet * set + (c % kBufsPerSet);
-            if (!mbar_wait(&tempty[buf], ((c / kBufsPerSet) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
+            const uint32_t buf = c % kBufs2;
+            if (!mbar_wait(&tempty[buf], ((c / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
               ok = false;
               fail(kStatusTimeoutMma);
               break;
@@ -735,7 +733,6 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           any = true;
           ring.next();
         }
-        if (set == 0) cnt0 = c; else if (set == 1) cnt1 = c; else if (set == 2) cnt2 = c; else cnt3 = c;
         if (!ok) break;
         // another block follows in this CTA's range: release the planes once these MMAs complete
         if (x < x_end && seg_at(P, x, x_end).u / kG2Slices != b) tc_commit(planes_empty);
@@ -748,59 +745,75 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ promotion
-    const int set = (warp - 4) >> 2;  // units ug with ug % 4 == set
-    const int ew = warp & 3;          // TMEM lane quarter
-    const int hrow = ew * 32 + lane;  // W2 row of the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    uint32_t cnt = 0;  // buffer uses of this set so far
+    // All 16 warps take every chunk: warp w reads TMEM lanes 32 (w % 4) .. +31 (its
+    // 32 W2 rows) and columns of token rows 4 tg .. 4 tg + 3, tg = (w - 4) / 4, of
+    // both planes; each thread accumulates its W2 row for those four tokens.
+    const int q4 = warp & 3;           // TMEM lane quarter
+    const int tg = (warp - 4) >> 2;    // token rows 4 tg .. 4 tg + 3
+    const int hrow = q4 * 32 + lane;   // W2 row of the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    uint32_t c = 0;  // buffer uses so far, in the MMA's order
     bool ok = true;
-    int ug = 0;
-    for (int x = x_beg; x < x_end && ok; ++ug) {
+    for (int x = x_beg; x < x_end && ok;) {
       const Seg sg = seg_at(P, x, x_end);
       x += sg.kb1 - sg.kb0;
       const int nk = sg.kb1 - sg.kb0;
-      if ((ug & (kSets - 1)) != set) continue;
       const int u = sg.u;
       const int4 blk = dbg_block(a.blocks[u / kG2Slices], BN, a.e_local, a.pcap, a.status);
       const int h = u % kG2Slices;
       const int e = blk.x, r0 = blk.y, nrows = blk.z;
       const float lane_scale = __ldg(a.w2_scale + ((size_t)e * kHBlocks + h) * kIBlocks + (lane & (kIBlocks - 1)));
-      float acc[BN];
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+        const float ws = __shfl_sync(0xffffffffu, lane_scale, kb);
+        float d[2][2][4];  // [chunk][plane][token]
+        uint32_t bufs[2];
 #pragma unroll
-      for (int t = 0; t < BN; ++t) acc[t] = 0.0f;
-      for (int l = 0; l < 2 * nk; ++l, ++cnt) {
-        const uint32_t buf = kBufsPerSet * set + (cnt % kBufsPerSet);
-        if (!mbar_wait(&tfull[buf], (cnt / kBufsPerSet) & 1u, sAbort, kWaitBudgetNs)) {
-          ok = false;
-          if (lane == 0) fail(kStatusTimeoutEpilogue);
-          break;
+        for (int ch = 0; ch < 2; ++ch, ++c) {
+          bufs[ch] = c % kBufs2;
+          if (!mbar_wait(&tfull[bufs[ch]], (c / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            if (lane == 0) fail(kStatusTimeoutEpilogue);
+            break;
+          }
         }
+        if (!ok) break;
         tc_fence_after();
-        const int chunk = 2 * sg.kb0 + l;  // 64-K chunk of the intermediate
-        const float ws = __shfl_sync(0xffffffffu, lane_scale, chunk >> 1);
-        float p0[16], p1[16];
-        tmem_ld16(tmem_base + lane_base + buf * kCols2, p0);
-        tmem_ld16(tmem_base + lane_base + buf * kCols2 + BN, p1);
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+          for (int pl = 0; pl < 2; ++pl)
+            tmem_ld4(tmem_base + lane_base + bufs[ch] * kCols2 + pl * BN + 4 * tg, d[ch][pl]);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
-        const float* s0 = sPScale + chunk;             // plane 0, row t: s0[t * kChunks]
-        const float* s1 = sPScale + BN * kChunks + chunk;
+        if (lane == 0) {
+          mbar_arrive(&tempty[bufs[0]]);
+          mbar_arrive(&tempty[bufs[1]]);
+        }
 #pragma unroll
-        for (int t = 0; t < BN; ++t) {
-          acc[t] = fmaf(p0[t], ws * s0[t * kChunks], acc[t]);
-          acc[t] = fmaf(p1[t], ws * s1[t * kChunks], acc[t]);
+        for (int ch = 0; ch < 2; ++ch) {
+          const int chunk = 2 * kb + ch;
+#pragma unroll
+          for (int pl = 0; pl < 2; ++pl) {
+            // this plane's scales of the chunk for token rows 4 tg .. 4 tg + 3
+            const float4 sv = *reinterpret_cast<const float4*>(sPScale + (pl * kChunks + chunk) * BN + 4 * tg);
+            const float sj[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] = fmaf(d[ch][pl][j], ws * sj[j], acc[j]);
+          }
         }
       }
       if (!ok) break;
+      (void)nk;
       const int sp = blockIdx.x - P.first_owner(u);  // segment index = plane of pair rows
       __half* dst = a.pair_out + (size_t)sp * a.plane_elems + (size_t)r0 * kHidden + h * 128 + hrow;
-      const float* wrow = a.row_weight + r0;
       bool sat = false;
 #pragma unroll
-      for (int t = 0; t < BN; ++t)
-        if (t < nrows) dst[(size_t)t * kHidden] = to_half_sat(acc[t] * __ldg(wrow + t), sat);
+      for (int j = 0; j < 4; ++j) {
+        const int t = 4 * tg + j;
+        if (t < nrows) dst[(size_t)t * kHidden] = to_half_sat(acc[j] * __ldg(a.row_weight + r0 + t), sat);
+      }
       if (sat) atomicOr(a.status, kStatusSaturated);
     }
   }
@@ -930,7 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     b2 += 2;
     for (int b = 0; b < kBufs2; ++b) {
       mbar_init(&b2[b], 1);
-      mbar_init(&b2[kBufs2 + b], 4);  // one arrive per warp of the promoting set
+      mbar_init(&b2[kBufs2 + b], 16);  // one arrive per promotion warp
     }
     mbar_init(&b2[2 * kBufs2], 1);
     *sAbort = 0;
@@ -1035,35 +1048,36 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   a.grid_extra = expire ? 1 : 0;
   a.grid_wait_ns = expire ? kTestGridWaitNs : kWaitBudgetNs;
   // Every CTA waits at the grid arrival for all the others, so the whole grid
-  // must be resident at once: one CTA per SM (the occupancy query confirms that
-  // one fits), launched cooperatively so that the launch itself guarantees it
-  // even when other work holds SMs.  The first launch on a device tries the
-  // cooperative launch with programmatic serialization, then without it; if the
-  // driver refuses both, the grid falls back to a plain launch sized by the
-  // occupancy query (the arrival wait is bounded either way).
+  // must be resident at once: one CTA per SM, and the occupancy query confirms
+  // that one fits.  The default launch is a plain programmatic one (its CTAs start
+  // while the router still runs; measured 1-3.5 us per call faster than a
+  // cooperative launch).  With FBMOE_DECODE_COOPERATIVE=1 the kernel is launched
+  // cooperatively, so that the launch itself guarantees co-residency even when
+  // other work holds SMs: with programmatic serialization if the driver accepts
+  // both, else without it.  The arrival wait is bounded either way.
   int occ = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel, kThreads, kSmemBytes);
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
   const int grid = num_sms > 0 ? num_sms : 1;
-  const int mode = g_decode_mode.load(std::memory_order_relaxed);
-  if (mode == 0 || mode == 1) {
-    e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, true, a);
-    if (e == cudaSuccess) {
-      g_decode_mode.store(1, std::memory_order_relaxed);
-      return e;
+  static const bool coop = [] {
+    const char* v = std::getenv("FBMOE_DECODE_COOPERATIVE");
+    return v != nullptr && v[0] == '1';
+  }();
+  if (coop) {
+    const int mode = g_decode_mode.load(std::memory_order_relaxed);
+    if (mode == 0 || mode == 1) {
+      e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, true, a);
+      if (e == cudaSuccess) {
+        g_decode_mode.store(1, std::memory_order_relaxed);
+        return e;
+      }
+      if (mode == 1) return e;
+      (void)cudaGetLastError();  // a refused launch configuration is not a sticky error
     }
-    if (mode == 1) return e;
-    (void)cudaGetLastError();  // a refused launch configuration is not a sticky error
-  }
-  if (mode == 0 || mode == 2) {
     e = launch_coop(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, false, a);
-    if (e == cudaSuccess) {
-      g_decode_mode.store(2, std::memory_order_relaxed);
-      return e;
-    }
-    if (mode == 2) return e;
-    (void)cudaGetLastError();
+    if (e == cudaSuccess) g_decode_mode.store(2, std::memory_order_relaxed);
+    return e;
   }
   g_decode_mode.store(3, std::memory_order_relaxed);
   return launch_pdl(decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, a);

@@ -42,12 +42,43 @@ def expire(fbmoe_lib):
     set_(False)
 
 
-def test_decode_kernel_launch_is_cooperative(fbmoe_lib, workloads, entry, case):
+def test_decode_kernel_launch_mode(fbmoe_lib, workloads, entry, case):
     entry.fused_moe(*workloads.as_args(case))
     torch.cuda.synchronize()
     mode = fbmoe_lib.decode_launch_mode()
     print("decode launch mode", mode)
-    assert mode in (1, 2), "the decode kernel's grid-wide arrival needs a cooperative launch"
+    want = (1, 2) if os.environ.get("FBMOE_DECODE_COOPERATIVE") == "1" else (3,)
+    assert mode in want
+
+
+def test_decode_kernel_cooperative_launch_in_a_child_process():
+    """FBMOE_DECODE_COOPERATIVE=1: the decode kernel is launched cooperatively (the launch guarantees that all its
+    CTAs are resident together) and gives the same output bits as the default launch."""
+    code = r"""
+import os, sys, torch
+sys.path.insert(0, os.path.join(os.environ["FBMOE_REPO"], "flashinfer-bench-moe_b200"))
+import fbmoe_lib as L, fbmoe_workloads as W
+w = W.make_weights(32, 5150, "cuda")
+inp = W.make_inputs(4, seed=8, config="group", device="cuda", weights=w)
+out = L.forward(*W.as_args(inp), sync_status=True)
+torch.save(out.cpu(), sys.argv[1])
+print("mode", L.decode_launch_mode())
+"""
+    import subprocess
+    import sys
+    import tempfile
+    from conftest import REPO
+    outs, modes = [], []
+    for coop in ("0", "1"):
+        with tempfile.NamedTemporaryFile(suffix=".pt") as f:
+            env = dict(os.environ, FBMOE_DECODE_COOPERATIVE=coop, FBMOE_REPO=REPO)
+            r = subprocess.run([sys.executable, "-c", code, f.name], env=env, capture_output=True, text=True,
+                               timeout=600)
+            assert r.returncode == 0, r.stderr[-2000:]
+            modes.append(int(r.stdout.strip().split()[-1]))
+            outs.append(torch.load(f.name))
+    assert modes[0] == 3 and modes[1] in (1, 2), modes
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
 
 
 def test_expired_wait_raises_with_sync_status(fbmoe_lib, workloads, entry, case, expire):
