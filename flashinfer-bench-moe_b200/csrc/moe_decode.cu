@@ -110,11 +110,15 @@ constexpr int kW2Prefetch = 24;
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kPlaneRows = 2 * BN;          // two planes of BN token rows
 constexpr int kPlaneKBytes = kPlaneRows * 128;
-constexpr int kBufs2 = 16;
+// K-block slots of tensor memory: a W2 tile's two 64-K chunks accumulate into the
+// slot's two 32-column halves, signalled by one commit per K-block (tcgen05.commit
+// is the expensive part of issuing at these sizes; the raw W2 stage is released by
+// the promotion warps once the slot's commit shows its MMAs done).
+constexpr int kSlots2 = 8;
 // Every promotion warp waits on every buffer use in order, so each parity wait is
 // for the phase right after the one the same waiter last saw (a parity wait cannot
 // alias a phase two completions ahead).
-constexpr int kCols2 = kPlaneRows;          // accumulator columns per buffer
+constexpr int kCols2 = kPlaneRows;          // accumulator columns per chunk (a slot holds two chunks)
 constexpr int kChunks = kInter / 64;         // 64-column chunks of the intermediate (plane scale blocks)
 constexpr int kP2Raw = 0;
 constexpr int kP2Planes = kP2Raw + kRawStages * kRawBytes;
@@ -123,7 +127,7 @@ constexpr int kP2End = kP2PScale + 2 * BN * kChunks * 4;
 constexpr int kRegion = ((kP1End > kP2End ? kP1End : kP2End) + 1023) / 1024 * 1024;
 // ---- barriers and flags (not reused across phases)
 constexpr int kNumBars1 = 2 * kStages1 + 2 * kBufs1 + 1;
-constexpr int kNumBars2 = 2 * kRawStages + 2 + 2 * kBufs2 + 1;
+constexpr int kNumBars2 = 2 * kRawStages + 2 + 2 * kSlots2 + 1;
 constexpr int kOffBar = kRegion;
 constexpr int kOffMisc = kOffBar + (kNumBars1 + kNumBars2) * 8;
 constexpr int kSmemBytes = kOffMisc + 32 + 1024;  // + alignment slack
@@ -131,7 +135,7 @@ constexpr int kTmemCols = 512;                    // one CTA per SM holds all of
 static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
 static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
 static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
-static_assert(kBufs1 * BN <= kTmemCols && kBufs2 * kCols2 <= kTmemCols, "TMEM allocation");
+static_assert(kBufs1 * BN <= kTmemCols && kSlots2 * 2 * kCols2 <= kTmemCols, "TMEM allocation");
 static_assert(kP2Planes % 1024 == 0, "the planes are 128-byte swizzle atoms");
 
 struct DecodeArgs {
@@ -592,12 +596,12 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
   uint8_t* sPlanes = sm + kP2Planes;
   const float* sPScale = reinterpret_cast<const float*>(sm + kP2PScale);  // [2 planes][32 chunks][16 rows]
   uint64_t* raw_full = bars;                  // W2 tile landed (TMA)
-  uint64_t* raw_empty = bars + SR;            // MMA done with it (tcgen05.commit)
+  uint64_t* raw_empty = bars + SR;            // MMA done with it (a promotion thread, after the slot's commit)
   uint64_t* planes_full = bars + 2 * SR;      // a block's planes and scales landed (TMA)
   uint64_t* planes_empty = planes_full + 1;   // MMA done with them (another block follows)
   uint64_t* tfull = planes_full + 2;
-  uint64_t* tempty = tfull + kBufs2;
-  uint64_t* drain = tempty + kBufs2;
+  uint64_t* tempty = tfull + kSlots2;
+  uint64_t* drain = tempty + kSlots2;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const Partition P = gemm2_partition(nb, a.streamk != 0);
@@ -688,7 +692,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(0u, 128, kCols2);  // e4m3 x e4m3
       Ring ring(SR);
-      uint32_t c = 0;  // buffer uses so far (two per K-block)
+      uint32_t c = 0;  // K-blocks so far (slot uses)
       int cur_blk = -1, nblk = 0;
       bool ok = true;
       bool any = false;
@@ -711,27 +715,26 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
             fail(kStatusTimeoutMma);
             break;
           }
+          const uint32_t slot = c % kSlots2;
+          if (!mbar_wait(&tempty[slot], ((c / kSlots2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
+            ok = false;
+            fail(kStatusTimeoutMma);
+            break;
+          }
+          tc_fence_after();
           const uint64_t adesc = umma_desc_sw128(smem_u32(sRaw + ring.slot * kRawBytes));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(sPlanes + kb * kPlaneKBytes));
-          // two 64-K chunks, each into its own buffer (promoted with its own plane scales)
+          // two 64-K chunks, each into its own half of the slot (promoted with its own plane scales)
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch, ++c) {
-            const uint32_t buf = c % kBufs2;
-            if (!mbar_wait(&tempty[buf], ((c / kBufs2) & 1u) ^ 1u, sAbort, kWaitBudgetNs)) {
-              ok = false;
-              fail(kStatusTimeoutMma);
-              break;
-            }
-            tc_fence_after();
-            const uint32_t d = tmem_base + buf * kCols2;
+          for (int ch = 0; ch < 2; ++ch) {
+            const uint32_t d = tmem_base + (slot * 2 + ch) * kCols2;
             mma_f8f6f4(d, adesc + 4 * ch, bdesc + 4 * ch, idesc, 0u);
             mma_f8f6f4(d, adesc + 4 * ch + 2, bdesc + 4 * ch + 2, idesc, 1u);
-            tc_commit(&tfull[buf]);
           }
-          if (!ok) break;
-          tc_commit(&raw_empty[ring.slot]);
+          tc_commit(&tfull[slot]);
           any = true;
           ring.next();
+          ++c;
         }
         if (!ok) break;
         // another block follows in this CTA's range: release the planes once these MMAs complete
@@ -752,7 +755,8 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     const int tg = (warp - 4) >> 2;    // token rows 4 tg .. 4 tg + 3
     const int hrow = q4 * 32 + lane;   // W2 row of the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    uint32_t c = 0;  // buffer uses so far, in the MMA's order
+    uint32_t c = 0;    // K-blocks so far, in the MMA's order
+    int rstage = 0;    // the raw W2 stage K-block c was read from
     bool ok = true;
     for (int x = x_beg; x < x_end && ok;) {
       const Seg sg = seg_at(P, x, x_end);
@@ -767,30 +771,26 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
       for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
         const float ws = __shfl_sync(0xffffffffu, lane_scale, kb);
         float d[2][2][4];  // [chunk][plane][token]
-        uint32_t bufs[2];
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch, ++c) {
-          bufs[ch] = c % kBufs2;
-          if (!mbar_wait(&tfull[bufs[ch]], (c / kBufs2) & 1u, sAbort, kWaitBudgetNs)) {
-            ok = false;
-            if (lane == 0) fail(kStatusTimeoutEpilogue);
-            break;
-          }
+        const uint32_t slot = c % kSlots2;
+        if (!mbar_wait(&tfull[slot], (c / kSlots2) & 1u, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          if (lane == 0) fail(kStatusTimeoutEpilogue);
+          break;
         }
-        if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
           for (int pl = 0; pl < 2; ++pl)
-            tmem_ld4(tmem_base + lane_base + bufs[ch] * kCols2 + pl * BN + 4 * tg, d[ch][pl]);
+            tmem_ld4(tmem_base + lane_base + (slot * 2 + ch) * kCols2 + pl * BN + 4 * tg, d[ch][pl]);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&tempty[bufs[0]]);
-          mbar_arrive(&tempty[bufs[1]]);
-        }
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+        // the slot's MMAs are complete, so the raw W2 stage they read is free (one thread signals)
+        if (threadIdx.x == 128) mbar_arrive(&raw_empty[rstage]);
+        rstage = rstage + 1 == kRawStages ? 0 : rstage + 1;
+        ++c;
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
           const int chunk = 2 * kb + ch;
@@ -935,17 +935,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     uint64_t* b2 = bars2;
     for (int s = 0; s < kRawStages; ++s) {
       mbar_init(&b2[s], 1);                // producer's expect_tx arrive
-      mbar_init(&b2[kRawStages + s], 1);   // tcgen05.commit
+      mbar_init(&b2[kRawStages + s], 1);   // one promotion thread, after the slot's commit
     }
     b2 += 2 * kRawStages;
     mbar_init(&b2[0], 1);  // the block's planes written (one arrive)
     mbar_init(&b2[1], 1);  // MMA done with them (tcgen05.commit)
     b2 += 2;
-    for (int b = 0; b < kBufs2; ++b) {
-      mbar_init(&b2[b], 1);
-      mbar_init(&b2[kBufs2 + b], 16);  // one arrive per promotion warp
+    for (int b = 0; b < kSlots2; ++b) {
+      mbar_init(&b2[b], 1);             // tcgen05.commit
+      mbar_init(&b2[kSlots2 + b], 16);  // one arrive per promotion warp
     }
-    mbar_init(&b2[2 * kBufs2], 1);
+    mbar_init(&b2[2 * kSlots2], 1);
     *sAbort = 0;
     fence_barrier_init();
   }
