@@ -135,7 +135,6 @@ constexpr int kTmemCols = 512;                    // one CTA per SM holds all of
 static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory over the per-CTA limit");
 static_assert(kHBlocks % kSets == 0, "K-blocks must split evenly over the epilogue sets");
 static_assert(kBufs1 % kSets == 0, "a buffer belongs to one epilogue set");
-static_assert(kStages1 % 2 == 0 && kBufs1 % 2 == 0, "GEMM1 stages and buffers are signalled in pairs");
 static_assert(kBufs1 * BN <= kTmemCols && kSlots2 * 2 * kCols2 <= kTmemCols, "TMEM allocation");
 static_assert(kP2Planes % 1024 == 0, "the planes are 128-byte swizzle atoms");
 
@@ -306,7 +305,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       const int wrow1 = e * kGemm1N + 64 * g;
       const int wrow2 = wrow1 + kInter;
       for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
-        if (!mbar_wait(&empty[stage >> 1], phase ^ 1u, sAbort, kWaitBudgetNs)) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, sAbort, kWaitBudgetNs)) {
           ok = false;
           if (lane == 0) fail(kStatusTimeoutProducer);
           break;
@@ -387,7 +386,6 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         x += sg.kb1 - sg.kb0;
         for (int l = 0; l < sg.kb1 - sg.kb0; ++l) {
           const uint32_t buf = kbg % kBufs1;
-          const bool last_kb = x >= x_end && l == sg.kb1 - sg.kb0 - 1;
           if (!mbar_wait(&tempty[buf], ((kbg / kBufs1) & 1u) ^ 1u, sAbort, kWaitBudgetNs) ||
               !mbar_wait(&full[stage], phase, sAbort, kWaitBudgetNs)) {
             ok = false;
@@ -400,12 +398,8 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
           const uint32_t d = tmem_base + buf * BN;
 #pragma unroll
           for (int j = 0; j < 4; ++j) mma_f8f6f4(d, adesc + 2 * j, bdesc + 2 * j, idesc, j > 0 ? 1u : 0u);
-          // tcgen05.commit is the costly part of issuing at N = 16: one commit per pair of
-          // K-blocks releases the pair of stages and signals the pair of TMEM buffers
-          if ((kbg & 1u) || last_kb) {
-            tc_commit(&empty[stage >> 1]);
-            tc_commit(&tfull[buf >> 1]);
-          }
+          tc_commit(&empty[stage]);
+          tc_commit(&tfull[buf]);
           any = true;
           ++kbg;
           if (++stage == S) {
@@ -462,7 +456,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       for (int l = (set - (int)(kbg % G) + G) % G; l < nk; l += G) {
         const uint32_t kgl = kbg + l;
         const uint32_t buf = kgl % kBufs1;
-        if (!mbar_wait(&tfull[buf >> 1], (kgl / kBufs1) & 1u, sAbort, kWaitBudgetNs)) {
+        if (!mbar_wait(&tfull[buf], (kgl / kBufs1) & 1u, sAbort, kWaitBudgetNs)) {
           bad = true;
           if (lane == 0) fail(kStatusTimeoutEpilogue);
           break;
