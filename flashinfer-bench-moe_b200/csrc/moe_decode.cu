@@ -103,10 +103,6 @@ constexpr int kP1End = kP1Tok + BN * 4;
 // plane 1, 16 token rows each) x 128 bytes, 128-byte swizzle, plus the planes'
 // fp32 scales.  Tensor memory: 16 accumulator buffers of 32 columns.
 constexpr int kRawStages = 9;
-// W2 tiles of its GEMM2 range a CTA asks L2 for when it has issued its last W1
-// load (384 KB per CTA, 57 MB over 148 CTAs: well inside the 126 MB L2), so
-// that HBM keeps streaming through the GEMM1 fix-ups and the hand-off to GEMM2.
-constexpr int kW2Prefetch = 24;
 constexpr int kRawBytes = 128 * 128;        // fp8 W2 tile
 constexpr int kPlaneRows = 2 * BN;          // two planes of BN token rows
 constexpr int kPlaneKBytes = kPlaneRows * 128;
@@ -341,19 +337,6 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
           stage = 0;
           phase ^= 1u;
         }
-      }
-    }
-    // GEMM2 streams this CTA's W2 tiles next: ask L2 for the first of them now.
-    if (lane == 0 && ok) {
-      const Partition P2 = gemm2_partition(nb, a.streamk != 0);
-      const int y_beg = P2.begin(blockIdx.x);
-      const int y_end = min(P2.begin(blockIdx.x + 1), y_beg + kW2Prefetch);
-      for (int y = y_beg; y < y_end;) {
-        const Seg sg = seg_at(P2, y, y_end);
-        y += sg.kb1 - sg.kb0;
-        const int4 blk = dbg_block(a.blocks[sg.u / kG2Slices], BN, a.e_local, a.pcap, a.status);
-        const int row = blk.x * kHidden + (sg.u % kG2Slices) * 128;
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb) tma_prefetch_l2_2d(&a.tm_w2, kb * kBlk, row);
       }
     }
     // complete the last kLag stages (or fewer)
