@@ -307,7 +307,8 @@ def run_ours(args, world, rank, local):
         # up to 20 % slower.  Let the clock recover, and record it for every sweep.
         time.sleep(SWEEP_SETTLE_S)
         for key, fn in (("decode_sweep", decode_sweep), ("quantiser", quantiser_point), ("prefill", prefill_points),
-                        ("prepack", prepack_points)):
+                        ("prepack", prepack_points),
+                        ("fp8_intermediate", lambda p: fp8_intermediate_points(p, inp))):
             with ClockSampler(local, interval_s=0.05) as sweep_clk:
                 line[key] = fn(peaks)
             line[key]["clocks"] = sweep_clk.summary()
@@ -352,11 +353,14 @@ def run_e2e(args, world, rank, inp, E_local, off, exchange=None, dispatch=False)
     (+ the EP combine) and copies this rank's output rows D2H.  Steps are pipelined the way a server would run
     them: two device buffer sets, H2D on one copy stream and D2H on another, so step i+1's upload and step i-1's
     download overlap step i's compute (PCIe is full duplex).  Timed on the compute stream from before the first
-    upload to after the last download.  dispatch=True: the token-dispatch layer, each rank uploading only its own
-    tokens' logits, fp8 rows and scales."""
+    upload to after the last download.  At N > 1 every token crosses PCIe once: each rank uploads only its own
+    T/N tokens' logits, fp8 rows and scales (the host's DMA bandwidth is shared by all the GPUs).  The
+    replicated-input layer then rebuilds all T tokens on every rank with an NVLink all-gather on the compute
+    stream (fbmoe_ep.TokenReplicator); dispatch=True runs the token-dispatch layer on the slices directly."""
     import fbmoe_lib as L
     names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
-    if dispatch:
+    rep, full = None, None
+    if world > 1:
         import fbmoe_ep
         lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
         src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
@@ -366,6 +370,9 @@ def run_e2e(args, world, rank, inp, E_local, off, exchange=None, dispatch=False)
     host = {k: src[k].cpu().contiguous().pin_memory() for k in names}
     dev = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device="cuda") for k in names} for _ in range(2)]
     w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+    if world > 1 and not dispatch:
+        rep = fbmoe_ep.TokenReplicator(T_EP)
+        full = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, device="cuda") for k in names if k != "routing_bias"}
     rows = T_EP // world
     out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
@@ -394,6 +401,10 @@ def run_e2e(args, world, rank, inp, E_local, off, exchange=None, dispatch=False)
         main.wait_event(ev_in[b])
         main.wait_event(ev_out[b])
         d = dev[b]
+        if rep is not None:
+            rep.gather(d["routing_logits"], d["hidden_states"], d["hidden_states_scale"], full["routing_logits"],
+                       full["hidden_states"], full["hidden_states_scale"])
+            d = dict(full, routing_bias=d["routing_bias"])
         if dispatch:
             exchange.forward_dispatch(d["routing_logits"], d["routing_bias"], d["hidden_states"],
                                       d["hidden_states_scale"], *w, inp["routed_scaling_factor"], out=out_dev[b])
@@ -429,7 +440,10 @@ def run_e2e(args, world, rank, inp, E_local, off, exchange=None, dispatch=False)
     ms = max_over_ranks(s.elapsed_time(e), world)
     return {"value": round(T_EP * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms / n, 4),
-            "pipelining": "2 buffer sets; H2D and D2H on their own streams overlap the neighbouring steps' compute"}
+            "pipelining": "2 buffer sets; H2D and D2H on their own streams overlap the neighbouring steps' compute",
+            "inputs": ("all T tokens uploaded" if world == 1 else
+                       "each rank uploads its T/N tokens" + ("" if dispatch else "; NVLink all-gather on the compute "
+                                                              "stream rebuilds the replicated inputs"))}
 
 
 def launches_per_forward(T, E_local, world=1, p2p=False):
@@ -548,6 +562,34 @@ def prepack_points(peaks):
                     "speedup": round(raw / pk, 4)})
     del packed, weights
     return {"what": "forward on raw W1 vs on fbmoe_prepack_w1 layout (one TMA box per GEMM1 tile)", "points": res}
+
+
+def fp8_intermediate_points(peaks, inp_ep):
+    """The fp8-intermediate mode (forward(intermediate="fp8"): the reference solution's re-quantised SwiGLU
+    output and an fp8 GEMM2) against the default f16 intermediate on the same inputs, timed alternately with L2
+    flushed between calls: config 2 at T = 4096 and 8192, and config 3 (the N = 1 benchmark step, T = 8192 over
+    all 256 experts).  Its accuracy is measured by tests/test_gpu_fp8_inter.py, not here."""
+    import fbmoe_lib as L
+    import fbmoe_workloads as W
+    weights = W.make_weights(32, 4242, "cuda")
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    cases = [(T, "config2_skew", W.as_args(W.make_inputs(T, seed=T, config="skew", device="cuda", weights=weights)))
+             for T in (4096, 8192)]
+    cases.append((T_EP, "config3_ep1", W.as_args(inp_ep)))
+    res = []
+    for T, name, args in cases:
+        f16 = time_calls(lambda: L.forward(*args, check=False), 6, lambda: flush_l2(buf))
+        fp8 = time_calls(lambda: L.forward(*args, check=False, intermediate="fp8"), 6, lambda: flush_l2(buf))
+        E = args[4].size(0)
+        idx, _ = L.route(args[0], args[1], args[9])
+        pairs = int(((idx >= args[8]) & (idx < args[8] + E)).sum().item())
+        tf = pairs * FLOPS_PER_PAIR / (fp8 / 1e3) / 1e12
+        res.append({"T": T, "config": name, "f16_us": round(f16 * 1e3, 1), "fp8_us": round(fp8 * 1e3, 1),
+                    "speedup": round(f16 / fp8, 4), "fp8_tflops": round(tf, 1),
+                    "fp8_frac_fp8_peak": round(tf / (2 * peaks["bf16_tflops"]), 4)})
+    del weights, cases
+    return {"what": "fp8-intermediate mode vs the default f16 intermediate (same inputs, alternated)",
+            "peak_note": "fp8 peak = 2x measured bf16 burst (both GEMMs fp8 in this mode)", "points": res}
 
 
 # --------------------------------------------------------------------------- CPU baselines

@@ -162,9 +162,23 @@ constexpr uint64_t kTestGridWaitNs = 2000000ull;
 // GEMM1 + SwiGLU for blocks of 128 rows with the tokens as the MMA M operand.
 // w1_packed: tm_w1 maps the fbmoe_prepack_w1 layout with 256-row boxes (one box per
 // operand tile) instead of the raw layout with 64-row boxes.
+// fp8_inter: the SwiGLU output is re-quantised to e4m3 with 1x128 scales (the
+// reference's numerics) into the intermediate region: e4m3 [pcap][2048] at
+// L.inter, fp32 scales [16][pcap] at L.inter + fp8_inter_scale_offset(L).
 cudaError_t launch_gemm1_rows(const CUtensorMap* tm_w1, const CUtensorMap* tm_aperm, const CUtensorMap* tm_ascale,
                               const float* w1_scale, const Layout& L, uint8_t* ws, int num_sms, bool w1_packed,
-                              cudaStream_t stream);
+                              cudaStream_t stream, bool fp8_inter = false);
+
+// Byte offset of the fp8 intermediate's scales inside the (f16-sized) intermediate region.
+inline size_t fp8_inter_scale_offset(const Layout& L) { return (size_t)L.pcap * 2048; }  // pcap rows of 2048 e4m3
+
+// GEMM2 of the fp8-intermediate mode: kind::f8f6f4 on the e4m3 intermediate
+// (tm_inter8, 128 x 128-byte boxes), its scales (tm_iscale, [16][pcap]) and raw W2
+// (tm_w2, 64-row x 128-byte boxes), promoted per 128-K block; f16 pair rows as
+// launch_gemm2_rows writes them (or scattered to the token owners).
+cudaError_t launch_gemm2_fp8_rows(const CUtensorMap* tm_w2, const CUtensorMap* tm_inter8,
+                                  const CUtensorMap* tm_iscale, const float* w2_scale, const Layout& L, uint8_t* ws,
+                                  int num_sms, cudaStream_t stream, const PeerScatter* scatter = nullptr);
 
 // GEMM2 for blocks of 128 rows with the tokens as the MMA M operand; tm_w2raw
 // maps W2 as unswizzled 64-byte x 256-row boxes.
@@ -185,6 +199,6 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
                  size_t workspace_bytes, void* stream, bool allow_split = true,
                  const PeerScatter* scatter = nullptr, const int32_t* routed_idx = nullptr,
-                 const float* routed_w = nullptr, bool w1_packed = false);
+                 const float* routed_w = nullptr, bool w1_packed = false, bool fp8_inter = false);
 
 }  // namespace fbmoe

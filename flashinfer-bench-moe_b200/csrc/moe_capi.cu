@@ -214,7 +214,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                  const void* gemm2_weights, const float* gemm2_weights_scale, int T, int E_local,
                  int local_expert_offset, float routed_scaling_factor, void* out, bool f32_out, void* workspace,
                  size_t workspace_bytes, void* stream_, bool allow_split, const PeerScatter* scatter,
-                 const int32_t* routed_idx, const float* routed_w, bool w1_packed) {
+                 const int32_t* routed_idx, const float* routed_w, bool w1_packed, bool fp8_inter) {
   if (T < 0 || E_local < 1 || E_local > kExperts) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
   const bool scattering = scatter != nullptr && scatter->world > 0;
@@ -225,7 +225,8 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
       !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || (!out && !scattering) || !workspace)
     return FBMOE_ERR_NULL_POINTER;
   if ((!routed && (!aligned(routing_logits, 16) || !aligned(routing_bias, 16))) || !aligned(hidden_states, 16) ||
-      !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(out, 16) || !aligned(workspace, 256))
+      !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(out, 16) || !aligned(workspace, 256) ||
+      !aligned(gemm1_weights_scale, 16) || !aligned(gemm2_weights_scale, 16))  // scale rows move by bulk copies
     return FBMOE_ERR_MISALIGNED;
   // the scatter lives in the row-major GEMM2's epilogue, so it forces that chain
   const int force_rows = scattering ? 128 : 0;
@@ -274,6 +275,20 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
                    (uint32_t)bn);
     if (rc) return rc;
   }
+  // fp8-intermediate mode (prefill chain): e4m3 intermediate rows in 128 x 128-byte boxes,
+  // their scales [16][pcap] in 128-row boxes of one K-block, raw W2 in 64-row boxes
+  const bool fp8_chain = fp8_inter && bn == 128;
+  CUtensorMap tm_inter8, tm_iscale, tm_w2b;
+  if (fp8_chain) {
+    rc = encode_2d(&tm_inter8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + L.inter, kInter, (uint64_t)L.pcap, 128, 128);
+    if (rc) return rc;
+    rc = encode_2d(&tm_iscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.inter + fp8_inter_scale_offset(L),
+                   (uint64_t)L.pcap, kIBlocks, 128, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = encode_2d(&tm_w2b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 128,
+                   64);
+    if (rc) return rc;
+  }
 
   int fwd = -1;
   if (g_prof.on) {
@@ -315,11 +330,16 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   } else {
     e = launch_gather_rows(reinterpret_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, L, ws, stream);
     if (e != cudaSuccess) return from_cuda(e);
-    e = launch_gemm1_rows(&tm_w1, &tm_aperm, &tm_ascale, gemm1_weights_scale, L, ws, sms, w1_packed, stream);
+    e = launch_gemm1_rows(&tm_w1, &tm_aperm, &tm_ascale, gemm1_weights_scale, L, ws, sms, w1_packed, stream,
+                          fp8_chain);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 3, stream);
-    e = launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream,
-                          scattering ? scatter : nullptr);
+    if (fp8_chain)
+      e = launch_gemm2_fp8_rows(&tm_w2b, &tm_inter8, &tm_iscale, gemm2_weights_scale, L, ws, sms, stream,
+                                scattering ? scatter : nullptr);
+    else
+      e = launch_gemm2_rows(&tm_w2raw, &tm_inter, gemm2_weights_scale, L, ws, sms, stream,
+                            scattering ? scatter : nullptr);
     if (e != cudaSuccess) return from_cuda(e);
     prof_record(fwd, 4, stream);
     // with the scatter, the owners' combine (moe_ep.cu) replaces the local reduce
@@ -341,6 +361,18 @@ int fbmoe_forward(const float* routing_logits, const void* routing_bias, const v
   return forward_core(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
                       routed_scaling_factor, out, false, workspace, workspace_bytes, stream);
+}
+
+int fbmoe_forward_fp8_intermediate(const float* routing_logits, const void* routing_bias, const void* hidden_states,
+                                   const float* hidden_states_scale, const void* gemm1_weights,
+                                   const float* gemm1_weights_scale, const void* gemm2_weights,
+                                   const float* gemm2_weights_scale, int T, int E_local, int local_expert_offset,
+                                   float routed_scaling_factor, void* out, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  return forward_core(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E_local, local_expert_offset,
+                      routed_scaling_factor, out, false, workspace, workspace_bytes, stream, true, nullptr, nullptr,
+                      nullptr, false, true);
 }
 
 int fbmoe_forward_partial_f32(const float* routing_logits, const void* routing_bias, const void* hidden_states,

@@ -8,9 +8,17 @@
 // -448, 448)) with round-to-nearest-even.  x / scale is an IEEE fp32 division, so
 // results are bit-identical to the same formula evaluated in fp32 on the host.
 //
-// One warp per (row, 8 consecutive blocks): 128 bf16 = 8 bytes per lane per
-// block, warp max by shuffles, one 4-byte store per lane per block.  HBM-bound:
+// One warp per task = (row, 8 consecutive blocks): each half-warp owns one block
+// per load (16 lanes x 16 B = 128 bf16), so a task is 4 loads of 16 B per lane,
+// half-warp max by 4 shuffles, one 8-byte store per lane per block pair.  The
+// next task's loads are issued before the current one is converted.  HBM-bound:
 // 14,336 B read + 7,168 B + 224 B written per row.
+//
+// Division: q needs e4m3(RN(x / s)) only.  y0 = RN(x * RN(1/s)) is within 3 fp32
+// ulps of RN(x / s); the two round to different e4m3 values only when the exact
+// quotient lies near an e4m3 rounding midpoint (the 20 mantissa bits below
+// e4m3's 3 equal 0x80000) or in e4m3's subnormal range, where the exact IEEE
+// division is taken instead.  Results stay bit-identical to x / s in fp32.
 #include "fbmoe.h"
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
@@ -20,49 +28,113 @@ namespace {
 
 constexpr int kWarps = 8;
 
-// Blocks per warp task: their loads are issued together, so each warp keeps
-// 8 x 256 B in flight (streaming needs ~100 KB in flight per SM).
+// Blocks per warp task (4 loads of 16 B per lane, 2 blocks per load).
 constexpr int kGroup = 8;
 static_assert(kHBlocks % kGroup == 0, "blocks per row must split into groups");
+constexpr int kLoads = kGroup / 2;
+
+// y0 is taken when its 20 mantissa bits below e4m3's 3 are at least 8 ulps away
+// from the rounding midpoint 0x80000 (the error bound is 3 ulps) and |y0| >= 2^-6,
+// e4m3's smallest normal, or y0 = +-0; a NaN y0 (a NaN input) fails the second test.  The
+// tests are branch-free and collected per lane into an 8-bit mask, so the exact
+// divisions cost one rarely taken branch per block.
+constexpr uint32_t kMidLow = 0x80000u;
+constexpr float kMinNormal = 0.015625f;  // 2^-6
+
+__device__ __forceinline__ uint32_t needs_exact(float y) {
+  const uint32_t u = __float_as_uint(y);
+  const uint32_t near_mid = ((u + 8u) & 0xFFFF0u) == kMidLow;  // low 20 bits in [0x7FFF8, 0x80007]
+  const uint32_t small = !(fabsf(y) >= kMinNormal || y == 0.0f);  // +-0 is exact (x = +-0)
+  return near_mid | small;
+}
+
+// The rare lanes whose mask is non-zero: the IEEE quotient for the flagged entries.
+__device__ __noinline__ void exact_quotients(const float* __restrict__ v, float s, uint32_t amb,
+                                             float* __restrict__ y) {
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i)
+    if ((amb >> i) & 1u) y[i] = __fdiv_rn(v[i], s);
+}
+
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ void load_task(const __nv_bfloat16* __restrict__ x, long task, long n_tasks, int lane,
+                                          uint4 (&v)[kLoads]) {
+  if (task >= n_tasks) return;
+  constexpr int kGroupsPerRow = kHBlocks / kGroup;
+  const int t = (int)(task / kGroupsPerRow), kb0 = (int)(task % kGroupsPerRow) * kGroup;
+  const __nv_bfloat16* p = x + (size_t)t * kHidden + (size_t)kb0 * kBlk + (lane >> 4) * kBlk + (lane & 15) * 8;
+#pragma unroll
+  for (int j = 0; j < kLoads; ++j) v[j] = __ldg(reinterpret_cast<const uint4*>(p + 2 * j * kBlk));
+}
 
 __global__ void __launch_bounds__(kWarps * 32) quant_act_kernel(const __nv_bfloat16* __restrict__ x, int T,
                                                                 uint8_t* __restrict__ q, float* __restrict__ scale) {
   const int lane = threadIdx.x & 31;
   constexpr int kGroupsPerRow = kHBlocks / kGroup;
   const long n_tasks = (long)T * kGroupsPerRow;
+  const long stride = (long)gridDim.x * kWarps;
   pdl_wait();
   pdl_trigger();
-  for (long task = (long)blockIdx.x * kWarps + (threadIdx.x >> 5); task < n_tasks; task += (long)gridDim.x * kWarps) {
+  long task = (long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  uint4 cur[kLoads], nxt[kLoads];
+  load_task(x, task, n_tasks, lane, cur);
+  for (; task < n_tasks; task += stride) {
+    load_task(x, task + stride, n_tasks, lane, nxt);
     const int t = (int)(task / kGroupsPerRow), kb0 = (int)(task % kGroupsPerRow) * kGroup;
-    const size_t base = (size_t)t * kHidden + (size_t)kb0 * kBlk + lane * 4;
-    uint2 raw[kGroup];
 #pragma unroll
-    for (int j = 0; j < kGroup; ++j) raw[j] = __ldg(reinterpret_cast<const uint2*>(x + base + j * kBlk));
-    float m[kGroup];
-#pragma unroll
-    for (int j = 0; j < kGroup; ++j) {
-      const float v0 = __uint_as_float(raw[j].x << 16), v1 = __uint_as_float(raw[j].x & 0xFFFF0000u);
-      const float v2 = __uint_as_float(raw[j].y << 16), v3 = __uint_as_float(raw[j].y & 0xFFFF0000u);
-      m[j] = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
-    }
-#pragma unroll
-    for (int d = 16; d >= 1; d >>= 1)
-#pragma unroll
-      for (int j = 0; j < kGroup; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(0xffffffffu, m[j], d));
-#pragma unroll
-    for (int j = 0; j < kGroup; ++j) {
-      const float s = m[j] > 0.0f ? __fdiv_rn(m[j], 448.0f) : 1.0f;
-      const float v[4] = {__uint_as_float(raw[j].x << 16), __uint_as_float(raw[j].x & 0xFFFF0000u),
-                          __uint_as_float(raw[j].y << 16), __uint_as_float(raw[j].y & 0xFFFF0000u)};
-      uint32_t packed = 0;
+    for (int j = 0; j < kLoads; ++j) {
+      const uint32_t w[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
+      float v[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float y = fminf(fmaxf(__fdiv_rn(v[i], s), -448.0f), 448.0f);
-        packed |= (uint32_t)__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3) << (8 * i);
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
       }
-      *reinterpret_cast<uint32_t*>(q + base + j * kBlk) = packed;
-      if (lane == j) scale[(size_t)(kb0 + j) * T + t] = s;
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+      for (int d = 8; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+      const float s = m > 0.0f ? __fdiv_rn(m, 448.0f) : 1.0f;
+      const float r = __frcp_rn(s);
+      const uint64_t rr = f32x2_pack(r, r);
+      float y[8];
+      uint32_t amb = (s >= 1.0e-36f && s <= 1.0e36f) ? 0u : 0xFFu;  // r = 1/s must be a finite normal number
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f32x2_unpack(mul_f32x2(f32x2_pack(v[2 * i], v[2 * i + 1]), rr), y[2 * i], y[2 * i + 1]);
+        amb |= (needs_exact(y[2 * i]) << (2 * i)) | (needs_exact(y[2 * i + 1]) << (2 * i + 1));
+      }
+      if (amb != 0u) {
+        float vt[8], yt[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          vt[i] = v[i];
+          yt[i] = y[i];
+        }
+        exact_quotients(vt, s, amb, yt);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = yt[i];
+      }
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t pair =
+            (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(y[2 * i], y[2 * i + 1]), __NV_SATFINITE, __NV_E4M3);
+        if (i < 2) lo |= pair << (16 * i);
+        else hi |= pair << (16 * (i - 2));
+      }
+      const int kb = kb0 + 2 * j + (lane >> 4);
+      *reinterpret_cast<uint2*>(q + (size_t)t * kHidden + (size_t)kb * kBlk + (lane & 15) * 8) = make_uint2(lo, hi);
+      if ((lane & 15) == 0) scale[(size_t)kb * T + t] = s;
     }
+#pragma unroll
+    for (int j = 0; j < kLoads; ++j) cur[j] = nxt[j];
   }
 }
 
@@ -73,10 +145,10 @@ extern "C" FBMOE_API int fbmoe_quantize_act(const void* x_bf16, int T, void* q_e
   if (T < 0) return FBMOE_ERR_INVALID_ARG;
   if (T == 0) return FBMOE_OK;
   if (!x_bf16 || !q_e4m3 || !scale) return FBMOE_ERR_NULL_POINTER;
-  if (((uintptr_t)x_bf16 & 7) || ((uintptr_t)q_e4m3 & 3)) return FBMOE_ERR_MISALIGNED;
+  if (((uintptr_t)x_bf16 & 15) || ((uintptr_t)q_e4m3 & 7)) return FBMOE_ERR_MISALIGNED;
   const long tasks = (long)T * (fbmoe::kHBlocks / fbmoe::kGroup);
   long blocks = (tasks + fbmoe::kWarps - 1) / fbmoe::kWarps;
-  if (blocks > 148L * 16) blocks = 148L * 16;
+  if (blocks > 148L * 8) blocks = 148L * 8;
   const cudaError_t e = fbmoe::launch_pdl(fbmoe::quant_act_kernel, dim3((unsigned)blocks), dim3(fbmoe::kWarps * 32),
                                           0, reinterpret_cast<cudaStream_t>(stream),
                                           reinterpret_cast<const __nv_bfloat16*>(x_bf16), T,

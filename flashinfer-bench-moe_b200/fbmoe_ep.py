@@ -70,6 +70,56 @@ def combine(partial_f32: torch.Tensor, group: Optional[dist.ProcessGroup] = None
     return out
 
 
+class TokenReplicator:
+    """Builds the replicated inputs of ``PeerExchange.forward`` from token-sharded ones: rank r holds rows
+    [r*T/N, (r+1)*T/N) of routing_logits [T, 256] and hidden_states [T, 7168] and the same columns of
+    hidden_states_scale [56, T]; after ``gather`` every rank holds all T tokens.
+
+    A host that feeds the layer uploads each token once (to the rank that holds it) and the ranks exchange
+    the slices over NVLink (one all-gather per tensor) instead of every rank uploading all T tokens over
+    PCIe.  Issue it on the stream that runs the layer: the collective then never shares the SMs with the
+    layer's persistent kernels.  Collective: every rank calls ``gather`` in the same order."""
+
+    def __init__(self, T: int, group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.T = int(T)
+        row_range(self.rank, self.world, self.T)  # validates T % world
+        self.rows = self.T // self.world
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
+                else torch.device("cpu")
+        self.device = device
+        # all_gather_into_tensor stacks slices along dim 0: the scale columns come back as [world, 56, T/N]
+        self._scale_stack = torch.empty((self.world, H // 128, self.rows), dtype=torch.float32, device=device)
+
+    def _gather(self, out: torch.Tensor, local: torch.Tensor) -> None:
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(out, local, group=self.group)
+        else:  # gloo has no all_gather_into_tensor
+            dist.all_gather(list(out.view((self.world,) + tuple(local.shape)).unbind(0)), local, group=self.group)
+
+    def gather(self, logits_local: torch.Tensor, hs_local: torch.Tensor, hs_scale_local: torch.Tensor,
+               logits: torch.Tensor, hs: torch.Tensor, hs_scale: torch.Tensor) -> None:
+        """Fill logits [T, 256], hs [T, 7168] and hs_scale [56, T] from every rank's slices."""
+        n, W = self.rows, self.world
+        if (tuple(logits_local.shape) != (n, E_TOTAL) or tuple(hs_local.shape) != (n, H)
+                or tuple(hs_scale_local.shape) != (H // 128, n)):
+            raise RuntimeError(f"slices must be [{n}, 256], [{n}, 7168] and [56, {n}]")
+        if (tuple(logits.shape) != (self.T, E_TOTAL) or tuple(hs.shape) != (self.T, H)
+                or tuple(hs_scale.shape) != (H // 128, self.T)):
+            raise RuntimeError(f"outputs must be [{self.T}, 256], [{self.T}, 7168] and [56, {self.T}]")
+        for t in (logits_local, hs_local, hs_scale_local, logits, hs, hs_scale):
+            if not t.is_contiguous():
+                raise RuntimeError("slices and outputs must be contiguous")
+        self._gather(logits, logits_local)
+        # fp8 rows travel as bytes (collectives of float8 types are not available on every backend)
+        self._gather(hs.view(torch.uint8), hs_local.view(torch.uint8))
+        self._gather(self._scale_stack, hs_scale_local)
+        hs_scale.view(H // 128, W, n).copy_(self._scale_stack.permute(1, 0, 2))
+
+
 def fused_moe_ep(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                  gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset: int,
                  routed_scaling_factor: float, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:

@@ -76,6 +76,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.fbmoe_prepack_w1.restype = i32
         lib.fbmoe_forward_prepacked.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, sz, vp]
         lib.fbmoe_forward_prepacked.restype = i32
+        lib.fbmoe_forward_fp8_intermediate.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp,
+                                                       sz, vp]
+        lib.fbmoe_forward_fp8_intermediate.restype = i32
         lib.fbmoe_error_string.argtypes = [i32]
         lib.fbmoe_error_string.restype = ctypes.c_char_p
         lib.fbmoe_version.argtypes = []
@@ -280,7 +283,8 @@ def check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scal
 def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
             gemm2_weights, gemm2_weights_scale, local_expert_offset, routed_scaling_factor,
             out: torch.Tensor = None, workspace: torch.Tensor = None, check: bool = True,
-            partial_f32: bool = False, sync_status: bool = None, w1_packed: bool = False) -> torch.Tensor:
+            partial_f32: bool = False, sync_status: bool = None, w1_packed: bool = False,
+            intermediate: str = "f16") -> torch.Tensor:
     """Run the fused MoE on the current stream; returns bf16 [T, 7168] (a fresh tensor unless `out` is given).
 
     With ``partial_f32`` the un-rounded fp32 sum over the local experts is returned
@@ -293,7 +297,11 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
     ``sync_status=True`` (or FBMOE_SYNC_STATUS=1) synchronises the stream after
     the launch and raises for this call itself.
 
-    ``w1_packed``: ``gemm1_weights`` is in the prepack_w1() layout (bf16 output only)."""
+    ``w1_packed``: ``gemm1_weights`` is in the prepack_w1() layout (bf16 output only).
+
+    ``intermediate="fp8"``: the reference's numerics for the prefill chain (T > 64): the SwiGLU output
+    re-quantised to e4m3 with 1x128 scales and GEMM2 on fp8 operands (fbmoe_forward_fp8_intermediate).  Faster,
+    but its re-quantisation error exceeds the operator's tolerance on some elements; bf16 output only."""
     lib = load_library()
     if check:
         T, E = check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
@@ -317,8 +325,14 @@ def forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         if word:
             raise DeviceStatusError(word, "reported by an earlier forward on this stream's workspace")
     _require(not (w1_packed and partial_f32), "w1_packed supports the bf16 output only")
-    fn = lib.fbmoe_forward_partial_f32 if partial_f32 else (
-        lib.fbmoe_forward_prepacked if w1_packed else lib.fbmoe_forward)
+    _require(intermediate in ("f16", "fp8"), "intermediate must be 'f16' or 'fp8'")
+    _require(intermediate == "f16" or not (partial_f32 or w1_packed),
+             "intermediate='fp8' supports raw weights and the bf16 output only")
+    if intermediate == "fp8":
+        fn = lib.fbmoe_forward_fp8_intermediate
+    else:
+        fn = lib.fbmoe_forward_partial_f32 if partial_f32 else (
+            lib.fbmoe_forward_prepacked if w1_packed else lib.fbmoe_forward)
     _check(fn(
         routing_logits.data_ptr(), routing_bias.data_ptr(), hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
         gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(), gemm2_weights.data_ptr(),

@@ -83,6 +83,22 @@ FBMOE_API int fbmoe_forward_partial_f32(const float* routing_logits, const void*
                                         int E_local, int local_expert_offset, float routed_scaling_factor,
                                         float* out_f32, void* workspace, size_t workspace_bytes, void* stream);
 
+/* fbmoe_forward with the reference's intermediate numerics: the SwiGLU output is
+ * re-quantised to e4m3 with 1x128 scales (amax / 448, act_quant_kernel,
+ * main.py:1426-1602) and GEMM2 multiplies fp8 by fp8 (gemm2_kernel,
+ * main.py:433-600), each 128-K block promoted in fp32.  Applies to the prefill
+ * chain (T > 64); smaller T run the decode kernel exactly as fbmoe_forward does.
+ * Same arguments, workspace and errors as fbmoe_forward.  Faster GEMM2 (fp8 rate,
+ * half the intermediate bytes) at the cost of the re-quantisation error, which
+ * exceeds the operator's atol 1e-2 / rtol 2e-2 on a fraction of the elements:
+ * not the default. */
+FBMOE_API int fbmoe_forward_fp8_intermediate(const float* routing_logits, const void* routing_bias,
+                                             const void* hidden_states, const float* hidden_states_scale,
+                                             const void* gemm1_weights, const float* gemm1_weights_scale,
+                                             const void* gemm2_weights, const float* gemm2_weights_scale, int T,
+                                             int E_local, int local_expert_offset, float routed_scaling_factor,
+                                             void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* fbmoe_forward for callers that cannot allocate device memory (no counterpart
  * in the reference).  Such callers -- a plugin host that hands over only input
  * and output pointers, a runtime whose allocator may not be called on this
@@ -143,7 +159,8 @@ FBMOE_API int fbmoe_route(const float* routing_logits, const void* routing_bias,
  * [56, T] (transposed, as the operator takes it).  Per row and 128-column block:
  * scale = amax / 448 (1 for an all-zero block), q = e4m3(clamp(x / scale, +-448)),
  * round-to-nearest-even -- the reference's 1x128 rule, solution/triton/main.py:
- * 1476-1488 (there applied to its SwiGLU output).  x 8-byte aligned, q 4-byte. */
+ * 1476-1488 (there applied to its SwiGLU output).  x 16-byte aligned, q 8-byte;
+ * values past +-448 saturate to +-448 and NaN stays NaN, as clamp then convert. */
 FBMOE_API int fbmoe_quantize_act(const void* x_bf16, int T, void* q_e4m3, float* scale, void* stream);
 
 /* Byte offsets of the forward's intermediate buffers inside the workspace, for

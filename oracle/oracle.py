@@ -162,10 +162,16 @@ def run(
     tokens: Optional[Sequence[int]] = None,
     routing=None,
     return_fp32: bool = False,
+    requant: bool = False,
 ) -> torch.Tensor:
     """The reference operator on CPU.  With ``tokens`` only those output rows are
     computed (each output row depends only on its own token), returned in the
-    given order as bf16 ``[len(tokens), H]``."""
+    given order as bf16 ``[len(tokens), H]``.
+
+    ``requant``: the reference solution's intermediate numerics instead of the
+    definition's fp32 -- the SwiGLU output re-quantised with the 1x128 rule
+    (act_quant_kernel, solution/triton/main.py:1476-1488) before GEMM2 (its fp8
+    gemm2_kernel, main.py:433-600), for checking the fp8-intermediate mode."""
     T = routing_logits.shape[0]
     E_local = gemm1_weights.shape[0]
     assert hidden_states.shape == (T, H)
@@ -204,6 +210,9 @@ def run(
         X1 = G1[:, :I]
         X2 = G1[:, I:]
         C = (X2 / (1.0 + torch.exp(-X2))) * X1
+        if requant:
+            q, sc = quantize_act_1x128(C)
+            C = q.to(torch.float32) * sc.t().repeat_interleave(BLOCK, dim=1)
         O = C.matmul(W2.t())
         out.index_add_(0, sel_t, O * w_tok.unsqueeze(1))
     return out if return_fp32 else out.to(torch.bfloat16)

@@ -142,3 +142,49 @@ def test_peer_exchange_setup_fails_on_every_rank_alike(fbmoe_lib):
         assert p.exitcode == 0
     assert got[0] == got[1] and got[0].startswith("peer exchange unavailable")
     assert "rank 0" in got[0] and "rank 1" in got[0]
+
+
+def _replicate_rank(rank, world, port, T, q):
+    import sys
+    sys.path.insert(0, PKG)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import fbmoe_ep
+        import fbmoe_workloads as W
+        logits, _, hs, hs_scale = W.make_activations(T, seed=11, config="standard", device="cpu")
+        lo, hi = fbmoe_ep.row_range(rank, world, T)
+        rep = fbmoe_ep.TokenReplicator(T, device=torch.device("cpu"))
+        out_l = torch.full_like(logits, float("nan"))
+        out_h = torch.zeros_like(hs)
+        out_s = torch.full_like(hs_scale, float("nan"))
+        rep.gather(logits[lo:hi].contiguous(), hs[lo:hi].contiguous(), hs_scale[:, lo:hi].contiguous(),
+                   out_l, out_h, out_s)
+        ok = (torch.equal(out_l, logits) and torch.equal(out_h.view(torch.uint8), hs.view(torch.uint8))
+              and torch.equal(out_s, hs_scale))
+        try:
+            rep.gather(logits[lo:hi], hs[lo:hi], hs_scale[:, lo:hi], out_l[:1], out_h, out_s)
+            bad_shape = "accepted"
+        except RuntimeError:
+            bad_shape = "rejected"
+        q.put((rank, ok, bad_shape))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,T", [(2, 64), (4, 96)])
+def test_token_replicator_rebuilds_the_replicated_inputs(world, T):
+    """Each rank holds T/N tokens (rows of logits and fp8 hidden states, columns of the [56, T] scales);
+    after the gather every rank holds all T tokens bit for bit (gloo ranks on CPU)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_replicate_rank, args=(r, world, port, T, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    assert sorted(r for r, _, _ in got) == list(range(world))
+    assert all(ok for _, ok, _ in got), got
+    assert all(b == "rejected" for _, _, b in got), got
