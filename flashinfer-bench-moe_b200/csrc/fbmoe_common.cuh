@@ -212,7 +212,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 // them marks the call as failed.
 __device__ __forceinline__ void forward_status_to_sink(uint32_t* status, uint32_t* sink) {
   if (sink == nullptr) return;
-  const uint32_t s = atomicOr(status, 0u);  // read at L2, after every earlier atomicOr
+  // A relaxed gpu-scope load reads the word at L2: it sees this CTA's own earlier
+  // atomicOr (ordered by the caller's CTA barrier) and whatever other CTAs have
+  // made visible; each CTA that sets a bit also forwards it at its own end.  (An
+  // atomicOr(status, 0) from every CTA would serialise at one L2 address.)
+  uint32_t s;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(s) : "l"(status) : "memory");
   if (s != 0u) {
     *reinterpret_cast<volatile uint32_t*>(sink) = s;
     __threadfence_system();
@@ -414,6 +419,46 @@ __device__ __forceinline__ void f32x2_unpack(uint64_t v, float& lo, float& hi) {
 }
 __device__ __forceinline__ void f32x2_fma(uint64_t& acc, uint64_t x, uint64_t y) {
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(x), "l"(y));
+}
+__device__ __forceinline__ uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ------------------------------------------- 1x128 e4m3 quantisation -------
+// e4m3(RN(a / s)) and e4m3(RN(b / s)), saturating, packed with a in the low
+// byte -- bit-identical to converting the IEEE quotients -- given the block's
+// E4m3Scale.  y0 = RN(x * r), r = RN(1 / s), lies within 3 fp32 ulps of
+// RN(x / s); the conversion is monotonic, so when y0 - 4 ulps and y0 + 4 ulps
+// convert to the same e4m3 value, so does RN(x / s).  Otherwise (an e4m3
+// rounding midpoint or zero within reach, NaN) the pair is divided exactly.  On
+// bf16 data about 0.5 % of the elements land that close to a midpoint (a short
+// ratio x / amax lands on one exactly).
+struct E4m3Scale {
+  float s;    // amax / 448 (1 for an all-zero block), the stored scale
+  float r;    // RN(1 / s)
+  bool fast;  // r is a finite normal number
+};
+__device__ __forceinline__ uint32_t e4m3x2_of(float a, float b) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ uint32_t e4m3x2_quotient(float a, float b, const E4m3Scale& q) {
+  float ya, yb;
+  f32x2_unpack(f32x2_mul(f32x2_pack(a, b), f32x2_pack(q.r, q.r)), ya, yb);
+  const uint32_t ua = __float_as_uint(ya), ub = __float_as_uint(yb);
+  const uint32_t lower = e4m3x2_of(__uint_as_float(ua - 4u), __uint_as_float(ub - 4u));
+  const uint32_t upper = e4m3x2_of(__uint_as_float(ua + 4u), __uint_as_float(ub + 4u));
+  if (lower == upper && q.fast) return lower;
+  return e4m3x2_of(__fdiv_rn(a, q.s), __fdiv_rn(b, q.s));
+}
+// The 1x128 rule's scale for a block with the given amax.
+__device__ __forceinline__ E4m3Scale e4m3_block_scale(float amax) {
+  E4m3Scale q;
+  q.s = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+  q.r = __frcp_rn(q.s);
+  q.fast = q.s >= 1.0e-36f && q.s <= 1.0e36f;
+  return q;
 }
 
 // Warp-collective TMEM load: 32 lanes x 4 consecutive fp32 columns.

@@ -390,16 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float bm = fmaxf(fmaxf(am[row], am[kRows + row]), fmaxf(am[2 * kRows + row], am[3 * kRows + row]));
         if (row < nrows) {
-          const float s = bm > 0.0f ? __fdiv_rn(bm, 448.0f) : 1.0f;
+          const E4m3Scale qs = e4m3_block_scale(bm);
+          const float s = qs.s;
           uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t lo = (uint32_t)__nv_cvt_float2_to_fp8x2(
-                make_float2(__fdiv_rn(y[4 * i], s), __fdiv_rn(y[4 * i + 1], s)), __NV_SATFINITE, __NV_E4M3);
-            const uint32_t hi = (uint32_t)__nv_cvt_float2_to_fp8x2(
-                make_float2(__fdiv_rn(y[4 * i + 2], s), __fdiv_rn(y[4 * i + 3], s)), __NV_SATFINITE, __NV_E4M3);
-            w[i] = lo | (hi << 16);
-          }
+          for (int i = 0; i < 8; ++i)
+            w[i] = e4m3x2_quotient(y[4 * i], y[4 * i + 1], qs) | (e4m3x2_quotient(y[4 * i + 2], y[4 * i + 3], qs) << 16);
           uint4* dst = reinterpret_cast<uint4*>(out.inter8 + (size_t)(r0 + row) * kInter + 128 * j + 32 * g);
           dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
           dst[1] = make_uint4(w[4], w[5], w[6], w[7]);

@@ -14,11 +14,10 @@
 // next task's loads are issued before the current one is converted.  HBM-bound:
 // 14,336 B read + 7,168 B + 224 B written per row.
 //
-// Division: q needs e4m3(RN(x / s)) only.  y0 = RN(x * RN(1/s)) is within 3 fp32
-// ulps of RN(x / s); the two round to different e4m3 values only when the exact
-// quotient lies near an e4m3 rounding midpoint (the 20 mantissa bits below
-// e4m3's 3 equal 0x80000) or in e4m3's subnormal range, where the exact IEEE
-// division is taken instead.  Results stay bit-identical to x / s in fp32.
+// Division: q needs e4m3(RN(x / s)) only, which e4m3x2_quotient (fbmoe_common.cuh)
+// gets from a multiplication by RN(1/s) and a bracketing conversion, dividing
+// exactly only near an e4m3 rounding midpoint; results stay bit-identical to
+// x / s in fp32.
 #include "fbmoe.h"
 #include "fbmoe_common.cuh"
 #include "fbmoe_launch.h"
@@ -32,35 +31,6 @@ constexpr int kWarps = 8;
 constexpr int kGroup = 8;
 static_assert(kHBlocks % kGroup == 0, "blocks per row must split into groups");
 constexpr int kLoads = kGroup / 2;
-
-// y0 is taken when its 20 mantissa bits below e4m3's 3 are at least 8 ulps away
-// from the rounding midpoint 0x80000 (the error bound is 3 ulps) and |y0| >= 2^-6,
-// e4m3's smallest normal, or y0 = +-0; a NaN y0 (a NaN input) fails the second test.  The
-// tests are branch-free and collected per lane into an 8-bit mask, so the exact
-// divisions cost one rarely taken branch per block.
-constexpr uint32_t kMidLow = 0x80000u;
-constexpr float kMinNormal = 0.015625f;  // 2^-6
-
-__device__ __forceinline__ uint32_t needs_exact(float y) {
-  const uint32_t u = __float_as_uint(y);
-  const uint32_t near_mid = ((u + 8u) & 0xFFFF0u) == kMidLow;  // low 20 bits in [0x7FFF8, 0x80007]
-  const uint32_t small = !(fabsf(y) >= kMinNormal || y == 0.0f);  // +-0 is exact (x = +-0)
-  return near_mid | small;
-}
-
-// The rare lanes whose mask is non-zero: the IEEE quotient for the flagged entries.
-__device__ __noinline__ void exact_quotients(const float* __restrict__ v, float s, uint32_t amb,
-                                             float* __restrict__ y) {
-#pragma unroll 1
-  for (int i = 0; i < 8; ++i)
-    if ((amb >> i) & 1u) y[i] = __fdiv_rn(v[i], s);
-}
-
-__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 
 __device__ __forceinline__ void load_task(const __nv_bfloat16* __restrict__ x, long task, long n_tasks, int lane,
                                           uint4 (&v)[kLoads]) {
@@ -100,32 +70,12 @@ __global__ void __launch_bounds__(kWarps * 32) quant_act_kernel(const __nv_bfloa
       for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
 #pragma unroll
       for (int d = 8; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
-      const float s = m > 0.0f ? __fdiv_rn(m, 448.0f) : 1.0f;
-      const float r = __frcp_rn(s);
-      const uint64_t rr = f32x2_pack(r, r);
-      float y[8];
-      uint32_t amb = (s >= 1.0e-36f && s <= 1.0e36f) ? 0u : 0xFFu;  // r = 1/s must be a finite normal number
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        f32x2_unpack(mul_f32x2(f32x2_pack(v[2 * i], v[2 * i + 1]), rr), y[2 * i], y[2 * i + 1]);
-        amb |= (needs_exact(y[2 * i]) << (2 * i)) | (needs_exact(y[2 * i + 1]) << (2 * i + 1));
-      }
-      if (amb != 0u) {
-        float vt[8], yt[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          vt[i] = v[i];
-          yt[i] = y[i];
-        }
-        exact_quotients(vt, s, amb, yt);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = yt[i];
-      }
+      const E4m3Scale qs = e4m3_block_scale(m);
+      const float s = qs.s;
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint32_t pair =
-            (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(y[2 * i], y[2 * i + 1]), __NV_SATFINITE, __NV_E4M3);
+        const uint32_t pair = e4m3x2_quotient(v[2 * i], v[2 * i + 1], qs);
         if (i < 2) lo |= pair << (16 * i);
         else hi |= pair << (16 * (i - 2));
       }
