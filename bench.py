@@ -661,6 +661,201 @@ def run_reference(args, world, rank):
     }
 
 
+# --------------------------------------------------------------------------- EP timeline (diagnosis)
+def copy_bandwidth(nbytes=64 << 20, reps=5):
+    """GB/s of H2D, D2H and both at once on separate streams, fresh pinned buffers, CUDA events."""
+    h_up = torch.ones(nbytes, dtype=torch.uint8).pin_memory()
+    h_down = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_up = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    d_down = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    res = {}
+    for name in ("h2d", "d2h", "duplex"):
+        t_up, t_down = [], []
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            if name != "d2h":
+                with torch.cuda.stream(up):
+                    ev[0].record()
+                    d_up.copy_(h_up, non_blocking=True)
+                    ev[1].record()
+            if name != "h2d":
+                with torch.cuda.stream(down):
+                    ev[2].record()
+                    h_down.copy_(d_down, non_blocking=True)
+                    ev[3].record()
+            torch.cuda.synchronize()
+            if name != "d2h":
+                t_up.append(ev[0].elapsed_time(ev[1]))
+            if name != "h2d":
+                t_down.append(ev[2].elapsed_time(ev[3]))
+        if t_up:
+            res[name + "_up_gbs"] = round(nbytes / (statistics.median(t_up) / 1e3) / 1e9, 1)
+        if t_down:
+            res[name + "_down_gbs"] = round(nbytes / (statistics.median(t_down) / 1e3) / 1e9, 1)
+    return res
+
+
+def e2e_timeline(world, rank, inp, exchange, mode, steps=10):
+    """run_e2e's pipelined loop with events on every stream per step.  mode: "dispatch" (token-sharded inputs),
+    "replicated_full" (every rank uploads all T tokens) or "replicated_sliced" (T/N uploaded, then
+    fbmoe_ep.TokenReplicator on the compute stream).  Times in ms from the first step's start."""
+    import fbmoe_ep
+    import fbmoe_lib as L
+    names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
+    if mode == "replicated_full":
+        src = {k: inp[k] for k in names}
+    else:
+        src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
+               "hidden_states": inp["hidden_states"][lo:hi],
+               "hidden_states_scale": inp["hidden_states_scale"][:, lo:hi]}
+    host = {k: src[k].cpu().contiguous().pin_memory() for k in names}
+    dev = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device="cuda") for k in names} for _ in range(2)]
+    rep, full = None, None
+    if mode == "replicated_sliced":
+        rep = fbmoe_ep.TokenReplicator(T_EP)
+        full = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, device="cuda") for k in names if k != "routing_bias"}
+    w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+    rows = T_EP // world
+    out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    main = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in, ev_used, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+    for i in range(2):
+        ev_used[i].record(main)
+        ev_out[i].record(main)
+    keys = ("up0", "up1", "c0", "gathered", "sent", "computed", "c1", "down0", "down1")
+    ev = [{k: torch.cuda.Event(enable_timing=True) for k in keys} for _ in range(steps + 2)]
+    host_ms = []
+    scale = inp["routed_scaling_factor"]
+
+    def one(i):
+        t0 = time.perf_counter()
+        b, x = i & 1, ev[i]
+        up.wait_event(ev_used[b])
+        with torch.cuda.stream(up):
+            x["up0"].record(up)
+            for k in names:
+                dev[b][k].copy_(host[k], non_blocking=True)
+            x["up1"].record(up)
+        ev_in[b].record(up)
+        main.wait_event(ev_in[b])
+        main.wait_event(ev_out[b])
+        x["c0"].record(main)
+        d = dev[b]
+        if rep is not None:
+            rep.gather(d["routing_logits"], d["hidden_states"], d["hidden_states_scale"], full["routing_logits"],
+                       full["hidden_states"], full["hidden_states_scale"])
+            d = dict(full, routing_bias=d["routing_bias"])
+        x["gathered"].record(main)
+        epoch = exchange._next_epoch()
+        if mode == "dispatch":
+            L.ep_dispatch_send(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"],
+                               T_EP, exchange.E_local, scale, rank, world, exchange.dispatch_ptrs, epoch,
+                               exchange.workspace)
+            x["sent"].record(main)
+            L.ep_dispatch_compute(*w, T_EP, rank, world, exchange.dispatch_local, exchange.ptrs, epoch,
+                                  exchange.workspace)
+        else:
+            x["sent"].record(main)
+            L.ep_send((d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w,
+                       exchange.offset, scale), rank, world, exchange.ptrs, epoch, exchange.workspace, check=False)
+        x["computed"].record(main)
+        L.ep_recv(exchange.local, T_EP, rank, world, epoch, out_dev[b], exchange.workspace)
+        x["c1"].record(main)
+        ev_used[b].record(main)
+        down.wait_event(ev_used[b])
+        with torch.cuda.stream(down):
+            x["down0"].record(down)
+            out_host[b].copy_(out_dev[b], non_blocking=True)
+            x["down1"].record(down)
+        ev_out[b].record(down)
+        host_ms.append((time.perf_counter() - t0) * 1e3)
+
+    for i in range(2):
+        one(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    host_ms.clear()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(main)
+    for i in range(2, steps + 2):
+        one(i)
+    main.wait_stream(down)
+    e.record(main)
+    torch.cuda.synchronize()
+    barrier(world)
+    tl = [{k: s.elapsed_time(v) for k, v in ev[i].items()} for i in range(2, steps + 2)]
+    med = lambda v: round(statistics.median(v), 3)  # noqa: E731
+    return {"rank": rank, "e2e_ms_per_step": round(s.elapsed_time(e) / steps, 3),
+            "upload": med([t["up1"] - t["up0"] for t in tl]),
+            "allgather": med([t["gathered"] - t["c0"] for t in tl]),
+            "dispatch_send": med([t["sent"] - t["gathered"] for t in tl]),
+            "experts_and_scatter": med([t["computed"] - t["sent"] for t in tl]),
+            "owner_combine": med([t["c1"] - t["computed"] for t in tl]),
+            "compute_step": med([t["c1"] - t["c0"] for t in tl]),
+            "download": med([t["down1"] - t["down0"] for t in tl]),
+            "gap_between_steps": med([tl[i]["c0"] - tl[i - 1]["c1"] for i in range(1, len(tl))]),
+            "host_enqueue": med(host_ms), "h2d_bytes": sum(v.numel() * v.element_size() for v in host.values()),
+            "status": exchange.status()}
+
+
+def run_ep_timeline(args):
+    """--case ep-timeline under torchrun (N >= 2): device-only steps of both EP layers, host copy bandwidth per
+    rank alone and all ranks at once, and the per-step stream timelines of the e2e loops; one JSON line."""
+    import torch.distributed as dist
+    import fbmoe_ep
+    world, rank, local = dist_setup()
+    if world < 2:
+        raise SystemExit("--case ep-timeline needs torchrun with 2 or more ranks")
+    inp, E_local, off = ep_inputs(world, rank)
+    exchange = fbmoe_ep.PeerExchange(T_EP, dispatch=True)
+    line = {"case": "ep-timeline", "n_gpus": world, "workload": workload_config(world), "host_cpus": os.cpu_count()}
+    lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
+    loc = (inp["routing_logits"][lo:hi].contiguous(), inp["routing_bias"], inp["hidden_states"][lo:hi].contiguous(),
+           inp["hidden_states_scale"][:, lo:hi].contiguous())
+    w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+    full = [inp[k] for k in ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")]
+    out = torch.empty((hi - lo, H), dtype=torch.bfloat16, device="cuda")
+    scale = inp["routed_scaling_factor"]
+    for name, fn in (("dispatch", lambda: exchange.forward_dispatch(*loc, *w, scale, out=out)),
+                     ("replicated", lambda: exchange.forward(*full, *w, scale, out=out, check=False))):
+        for _ in range(args.warmup):
+            fn()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            fn()
+        e.record()
+        barrier(world)
+        line[f"device_{name}_ms_per_step"] = round(max_over_ranks(s.elapsed_time(e), world) / args.steps, 4)
+    alone = None
+    for r in range(world):
+        barrier(world)
+        if rank == r:
+            alone = copy_bandwidth()
+        barrier(world)
+    together = copy_bandwidth()
+    barrier(world)
+    objs = [None] * world
+    dist.all_gather_object(objs, {"rank": rank, "alone": alone, "all_ranks_at_once": together})
+    line["copy_gbs"] = objs
+    for mode in ("dispatch", "replicated_full", "replicated_sliced"):
+        r = e2e_timeline(world, rank, inp, exchange, mode, steps=max(3, min(args.steps, 10)))
+        objs = [None] * world
+        dist.all_gather_object(objs, r)
+        line["e2e_" + mode] = objs
+    exchange.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_case(args):
     """One config at one T on GPU 0 (used for profiling captures): decode = config 1,
     prefill = config 2 (skewed routing); 32 local experts, L2 flushed between calls."""
@@ -704,13 +899,18 @@ def main():
                          "NCCL reduce-scatter (nccl)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--case", choices=("ep", "decode", "prefill", "shard"), default="ep",
+    ap.add_argument("--case", choices=("ep", "decode", "prefill", "shard", "ep-timeline"), default="ep",
                     help="ep = the benchmark line (default); decode/prefill/shard = one small config for profiling "
-                         "(shard = uniform routing over 32 local experts: one rank's work at N=8 when T=8192)")
+                         "(shard = uniform routing over 32 local experts: one rank's work at N=8 when T=8192); "
+                         "ep-timeline = per-rank stream timelines of the e2e loops and host copy bandwidth "
+                         "(torchrun, N >= 2)")
     ap.add_argument("--T", type=int, default=64, help="tokens for --case decode/prefill")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.case == "ep-timeline":
+        run_ep_timeline(args)
+        return
     if args.case != "ep":
         run_case(args)
         return

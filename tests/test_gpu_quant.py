@@ -30,3 +30,23 @@ def test_quantize_act_bit_exact(oracle_mod, fbmoe_lib, T, seed):
 def test_quantize_act_rejects_bad_input(fbmoe_lib):
     with pytest.raises(RuntimeError):
         fbmoe_lib.quantize_act(torch.zeros((4, 7168), dtype=torch.float32, device="cuda"))
+
+
+def test_quantize_act_bit_exact_on_rounding_midpoints(oracle_mod, fbmoe_lib):
+    """Blocks built so that many x / scale land on (or next to) e4m3 rounding midpoints: x = amax * k / 64 and
+    amax * k / 56 with amax a power of two or 7 * 2^j.  The kernel's reciprocal path must hand these to the
+    exact division and still match the oracle's IEEE division bit for bit."""
+    g = torch.Generator().manual_seed(99)
+    T = 512
+    k = torch.randint(-64, 65, (T, 7168), generator=g).float()
+    amax = torch.tensor([1.0, 8.0, 7.0, 0.875, 3.5, 1.75e-3, 2.0 ** 20, 5.0])[torch.arange(T * 56) % 8]
+    amax = amax.view(T, 56).repeat_interleave(128, dim=1)
+    denom = torch.where(torch.arange(7168) % 2 == 0, torch.tensor(64.0), torch.tensor(56.0))
+    x = (amax * k / denom)
+    x[:, ::128] = amax[:, ::128]          # every block reaches its amax exactly
+    x = x.to(torch.bfloat16)
+    q, s = fbmoe_lib.quantize_act(x.cuda())
+    torch.cuda.synchronize()
+    q_ref, s_ref = oracle_mod.quantize_act_1x128(x)
+    assert torch.equal(s.cpu(), s_ref)
+    assert torch.equal(q.cpu().view(torch.uint8), q_ref.view(torch.uint8))
