@@ -278,10 +278,20 @@ def run_ours(args, world, rank, local):
                 "stage_ms_per_step": {k: round(v, 4) for k, v in per_stage.items()}, "local_pairs": pairs,
                 "active_local_experts": active}
 
-    e2e = run_e2e(args, world, rank, inp, E_local, off, exchange)
+    if world == 1:
+        e2e = run_e2e(args, world, rank, inp, "single")
+    elif exchange is None:
+        e2e = run_e2e(args, world, rank, inp, "nccl")
+    else:
+        # replicated inputs from the host: every rank uploading all T tokens, or each rank its T/N tokens plus
+        # an NVLink all-gather; the line reports the faster plan and keeps the other beside it
+        plans = [run_e2e(args, world, rank, inp, m, exchange) for m in ("replicated_full", "replicated_sliced")]
+        e2e = dict(min(plans, key=lambda r: r["ms_per_step"]))
+        e2e["plans"] = {r["mode"]: {"ms_per_step": r["ms_per_step"], "h2d_bytes_per_step": r["h2d_bytes_per_step"]}
+                        for r in plans}
     dispatch = run_dispatch(args, world, rank, inp, exchange) if exchange is not None else None
     if dispatch is not None:
-        dispatch["e2e"] = run_e2e(args, world, rank, inp, E_local, off, exchange, dispatch=True)
+        dispatch["e2e"] = run_e2e(args, world, rank, inp, "dispatch", exchange)
     if fallback is not None:
         dispatch = {"unavailable": fallback}
     if exchange is not None:
@@ -348,102 +358,184 @@ def run_dispatch(args, world, rank, inp, exchange):
             "gpu_launches_per_step": launches_per_forward(T_EP, E_TOTAL // world, world, True) + 3}
 
 
-def run_e2e(args, world, rank, inp, E_local, off, exchange=None, dispatch=False):
-    """Public API with host buffers: every step copies its activations H2D from pinned memory, runs fused_moe
-    (+ the EP combine) and copies this rank's output rows D2H.  Steps are pipelined the way a server would run
-    them: two device buffer sets, H2D on one copy stream and D2H on another, so step i+1's upload and step i-1's
-    download overlap step i's compute (PCIe is full duplex).  Timed on the compute stream from before the first
-    upload to after the last download.  At N > 1 every token crosses PCIe once: each rank uploads only its own
-    T/N tokens' logits, fp8 rows and scales (the host's DMA bandwidth is shared by all the GPUs).  The
-    replicated-input layer then rebuilds all T tokens on every rank with an NVLink all-gather on the compute
-    stream (fbmoe_ep.TokenReplicator); dispatch=True runs the token-dispatch layer on the slices directly."""
-    import fbmoe_lib as L
-    names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
-    rep, full = None, None
-    if world > 1:
-        import fbmoe_ep
-        lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
-        src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
-               "hidden_states": inp["hidden_states"][lo:hi], "hidden_states_scale": inp["hidden_states_scale"][:, lo:hi]}
-    else:
-        src = {k: inp[k] for k in names}
-    host = {k: src[k].cpu().contiguous().pin_memory() for k in names}
-    dev = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device="cuda") for k in names} for _ in range(2)]
-    w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
-    if world > 1 and not dispatch:
-        rep = fbmoe_ep.TokenReplicator(T_EP)
-        full = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, device="cuda") for k in names if k != "routing_bias"}
-    rows = T_EP // world
-    out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = out_host[0].numel() * out_host[0].element_size()
-    if world > 1 and exchange is None:
-        import fbmoe_ep
-        partial = torch.empty((T_EP, H), dtype=torch.float32, device="cuda")
-        shard = torch.empty((rows, H), dtype=torch.float32, device="cuda")
-    main = torch.cuda.current_stream()
-    up, down = torch.cuda.Stream(), torch.cuda.Stream()
-    ev_in = [torch.cuda.Event() for _ in range(2)]        # inputs of the slot uploaded
-    ev_used = [torch.cuda.Event() for _ in range(2)]      # compute done reading the slot's inputs / writing its output
-    ev_out = [torch.cuda.Event() for _ in range(2)]       # the slot's output downloaded
-    for i in range(2):
-        ev_used[i].record(main)
-        ev_out[i].record(main)
+class E2ELoop:
+    """The pipelined host-buffer loop of the e2e measurements.  Every step copies its activations H2D from pinned
+    memory, runs the layer and copies this rank's output rows D2H, the way a server would run it: two device
+    buffer sets, uploads on one copy stream and downloads on another, overlapping the neighbouring steps' compute.
 
-    def one(i):
-        b = i & 1
-        up.wait_event(ev_used[b])
-        with torch.cuda.stream(up):
-            for k in names:
-                dev[b][k].copy_(host[k], non_blocking=True)
-        ev_in[b].record(up)
-        main.wait_event(ev_in[b])
-        main.wait_event(ev_out[b])
-        d = dev[b]
-        if rep is not None:
-            rep.gather(d["routing_logits"], d["hidden_states"], d["hidden_states_scale"], full["routing_logits"],
-                       full["hidden_states"], full["hidden_states_scale"])
-            d = dict(full, routing_bias=d["routing_bias"])
-        if dispatch:
-            exchange.forward_dispatch(d["routing_logits"], d["routing_bias"], d["hidden_states"],
-                                      d["hidden_states_scale"], *w, inp["routed_scaling_factor"], out=out_dev[b])
-        elif world == 1:
-            L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w, off,
-                      inp["routed_scaling_factor"], out=out_dev[b])
-        elif exchange is not None:
-            exchange.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w,
-                             inp["routed_scaling_factor"], out=out_dev[b])
+    mode: "single" (N = 1, fused_moe), "replicated_full" (every rank uploads all T tokens), "replicated_sliced"
+    (each rank uploads its T/N tokens; fbmoe_ep.TokenReplicator rebuilds all T on the compute stream),
+    "dispatch" (token-dispatch layer on the rank's T/N tokens) or "nccl" (fp32 partial + reduce-scatter).
+
+    Host copies slow a concurrent NVLink exchange several-fold (measured at N = 4: the dispatch send 0.14 ->
+    0.4-0.6 ms, the NCCL all-gather 0.19 -> 1.13 ms).  In the two modes that open a step with an exchange (the
+    dispatch send, the all-gather) the copies are therefore ordered after it: step i+1's upload and step i-1's
+    download start once step i's exchange is done and overlap the rest of its compute."""
+
+    def __init__(self, world, rank, inp, exchange, mode):
+        import fbmoe_ep
+        import fbmoe_lib as L
+        self.L, self.world, self.rank, self.inp, self.exchange, self.mode = L, world, rank, inp, exchange, mode
+        self.names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+        if mode in ("replicated_sliced", "dispatch"):
+            lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
+            src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
+                   "hidden_states": inp["hidden_states"][lo:hi],
+                   "hidden_states_scale": inp["hidden_states_scale"][:, lo:hi]}
         else:
-            L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w, off,
-                      inp["routed_scaling_factor"], out=partial, partial_f32=True)
-            fbmoe_ep.combine(partial, out=out_dev[b], scratch=shard)
-        ev_used[b].record(main)
-        down.wait_event(ev_used[b])
-        with torch.cuda.stream(down):
-            out_host[b].copy_(out_dev[b], non_blocking=True)
-        ev_out[b].record(down)
+            src = {k: inp[k] for k in self.names}
+        self.host = {k: src[k].cpu().contiguous().pin_memory() for k in self.names}
+        self.dev = [{k: torch.empty(v.shape, dtype=v.dtype, device="cuda") for k, v in self.host.items()}
+                    for _ in range(2)]
+        self.w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
+        rows = T_EP // world
+        self.out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        self.out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+        self.h2d = sum(v.numel() * v.element_size() for v in self.host.values())
+        self.d2h = self.out_host[0].numel() * self.out_host[0].element_size()
+        self.rep = self.full = None
+        if mode == "replicated_sliced":
+            self.rep = fbmoe_ep.TokenReplicator(T_EP)
+            self.full = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, device="cuda")
+                         for k in self.names if k != "routing_bias"}
+        if mode == "nccl":
+            self.partial = torch.empty((T_EP, H), dtype=torch.float32, device="cuda")
+            self.shard = torch.empty((rows, H), dtype=torch.float32, device="cuda")
+        self.gate = mode in ("replicated_sliced", "dispatch")
+        self.main = torch.cuda.current_stream()
+        self.up, self.down = torch.cuda.Stream(), torch.cuda.Stream()
+        self.ev_in = [torch.cuda.Event() for _ in range(2)]    # the slot's inputs uploaded
+        self.ev_used = [torch.cuda.Event() for _ in range(2)]  # compute done with the slot
+        self.ev_out = [torch.cuda.Event() for _ in range(2)]   # the slot's output downloaded
+        self.ev_x = [torch.cuda.Event() for _ in range(2)]     # the step's exchange phase done
+        for i in range(2):
+            self.ev_used[i].record(self.main)
+            self.ev_out[i].record(self.main)
+        self.pending = None  # (slot, marks) whose download waits for the next step's exchange
 
-    n = max(3, min(args.steps, 10))
+    def _download(self, b, marks, after_x=None):
+        self.down.wait_event(self.ev_used[b])
+        if after_x is not None:
+            self.down.wait_event(after_x)
+        with torch.cuda.stream(self.down):
+            _mark(marks, "down0", self.down)
+            self.out_host[b].copy_(self.out_dev[b], non_blocking=True)
+            _mark(marks, "down1", self.down)
+        self.ev_out[b].record(self.down)
+
+    def step(self, i, marks=None):
+        L, main, b = self.L, self.main, i & 1
+        self.up.wait_event(self.ev_used[b])
+        if self.gate and i > 0:
+            self.up.wait_event(self.ev_x[(i - 1) & 1])
+        with torch.cuda.stream(self.up):
+            _mark(marks, "up0", self.up)
+            for k in self.names:
+                self.dev[b][k].copy_(self.host[k], non_blocking=True)
+            _mark(marks, "up1", self.up)
+        self.ev_in[b].record(self.up)
+        main.wait_event(self.ev_in[b])
+        main.wait_event(self.ev_out[b])
+        _mark(marks, "c0", main)
+        d, ex, scale = self.dev[b], self.exchange, self.inp["routed_scaling_factor"]
+        epoch = ex._next_epoch() if ex is not None else 0
+        if self.rep is not None:
+            self.rep.gather(d["routing_logits"], d["hidden_states"], d["hidden_states_scale"],
+                            self.full["routing_logits"], self.full["hidden_states"], self.full["hidden_states_scale"])
+            d = dict(self.full, routing_bias=d["routing_bias"])
+        if self.mode == "dispatch":
+            L.ep_dispatch_send(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"],
+                               T_EP, ex.E_local, scale, self.rank, self.world, ex.dispatch_ptrs, epoch, ex.workspace)
+        self.ev_x[b].record(main)
+        _mark(marks, "exchanged", main)
+        if self.pending is not None:
+            self._download(*self.pending, after_x=self.ev_x[b])
+            self.pending = None
+        if self.mode == "single":
+            L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *self.w,
+                      self.inp["local_expert_offset"], scale, out=self.out_dev[b], check=False)
+            _mark(marks, "computed", main)
+        elif self.mode == "nccl":
+            import fbmoe_ep
+            L.forward(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *self.w,
+                      self.inp["local_expert_offset"], scale, out=self.partial, partial_f32=True, check=False)
+            _mark(marks, "computed", main)
+            fbmoe_ep.combine(self.partial, out=self.out_dev[b], scratch=self.shard)
+        else:
+            if self.mode == "dispatch":
+                L.ep_dispatch_compute(*self.w, T_EP, self.rank, self.world, ex.dispatch_local, ex.ptrs, epoch,
+                                      ex.workspace)
+            else:
+                L.ep_send((d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"],
+                           *self.w, ex.offset, scale), self.rank, self.world, ex.ptrs, epoch, ex.workspace,
+                          check=False)
+            _mark(marks, "computed", main)
+            L.ep_recv(ex.local, T_EP, self.rank, self.world, epoch, self.out_dev[b], ex.workspace)
+        _mark(marks, "c1", main)
+        self.ev_used[b].record(main)
+        if self.gate:
+            self.pending = (b, marks)
+        else:
+            self._download(b, marks)
+
+    def flush(self):
+        if self.pending is not None:
+            self._download(*self.pending)
+            self.pending = None
+        self.main.wait_stream(self.down)
+
+
+def _mark(marks, key, stream):
+    if marks is not None:
+        marks[key].record(stream)
+
+
+E2E_MARKS = ("up0", "up1", "c0", "exchanged", "computed", "c1", "down0", "down1")
+
+
+def run_e2e(args, world, rank, inp, mode, exchange=None, steps=None, instrument=False):
+    """e2e of the layer through the public API with host buffers (E2ELoop), timed on the compute stream from before
+    the first upload to after the last download; max over ranks.  instrument: also per-step stream timelines."""
+    loop = E2ELoop(world, rank, inp, exchange, mode)
+    n = steps if steps is not None else max(3, min(args.steps, 10))
     for i in range(2):
-        one(i)
+        loop.step(i)
+    loop.flush()
     torch.cuda.synchronize()
     barrier(world)
+    marks = [{k: torch.cuda.Event(enable_timing=True) for k in E2E_MARKS} for _ in range(n)] if instrument else None
+    host_ms = []
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(main)
+    s.record(loop.main)
     for i in range(n):
-        one(i)
-    main.wait_stream(down)
-    e.record(main)
+        t0 = time.perf_counter()
+        loop.step(2 + i, marks[i] if instrument else None)
+        host_ms.append((time.perf_counter() - t0) * 1e3)
+    loop.flush()
+    e.record(loop.main)
     torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(s.elapsed_time(e), world)
-    return {"value": round(T_EP * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms / n, 4),
-            "pipelining": "2 buffer sets; H2D and D2H on their own streams overlap the neighbouring steps' compute",
-            "inputs": ("all T tokens uploaded" if world == 1 else
-                       "each rank uploads its T/N tokens" + ("" if dispatch else "; NVLink all-gather on the compute "
-                                                              "stream rebuilds the replicated inputs"))}
+    own = s.elapsed_time(e)
+    ms = max_over_ranks(own, world)
+    res = {"value": round(T_EP * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": loop.h2d,
+           "d2h_bytes_per_step": loop.d2h, "steps": n, "ms_per_step": round(ms / n, 4), "mode": mode,
+           "pipelining": "2 buffer sets; H2D and D2H on their own streams overlap the neighbouring steps' compute"
+                         + ("; copies ordered after the step's NVLink exchange" if loop.gate else "")}
+    if instrument:
+        tl = [{k: s.elapsed_time(v) for k, v in m.items()} for m in marks]
+        med = lambda v: round(statistics.median(v), 3)  # noqa: E731
+        res["timeline"] = {
+            "rank": rank, "own_ms_per_step": round(own / n, 3), "upload": med([t["up1"] - t["up0"] for t in tl]),
+            "exchange": med([t["exchanged"] - t["c0"] for t in tl]),
+            "experts": med([t["computed"] - t["exchanged"] for t in tl]),
+            "owner_combine": med([t["c1"] - t["computed"] for t in tl]),
+            "compute_step": med([t["c1"] - t["c0"] for t in tl]),
+            "download": med([t["down1"] - t["down0"] for t in tl]),
+            "gap_between_steps": med([tl[i]["c0"] - tl[i - 1]["c1"] for i in range(1, len(tl))]),
+            "host_enqueue": med(host_ms)}
+        if exchange is not None:
+            res["timeline"]["status"] = exchange.status()
+    return res
 
 
 def launches_per_forward(T, E_local, world=1, p2p=False):
@@ -697,115 +789,10 @@ def copy_bandwidth(nbytes=64 << 20, reps=5):
     return res
 
 
-def e2e_timeline(world, rank, inp, exchange, mode, steps=10):
-    """run_e2e's pipelined loop with events on every stream per step.  mode: "dispatch" (token-sharded inputs),
-    "replicated_full" (every rank uploads all T tokens) or "replicated_sliced" (T/N uploaded, then
-    fbmoe_ep.TokenReplicator on the compute stream).  Times in ms from the first step's start."""
-    import fbmoe_ep
-    import fbmoe_lib as L
-    names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
-    lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
-    if mode == "replicated_full":
-        src = {k: inp[k] for k in names}
-    else:
-        src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
-               "hidden_states": inp["hidden_states"][lo:hi],
-               "hidden_states_scale": inp["hidden_states_scale"][:, lo:hi]}
-    host = {k: src[k].cpu().contiguous().pin_memory() for k in names}
-    dev = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device="cuda") for k in names} for _ in range(2)]
-    rep, full = None, None
-    if mode == "replicated_sliced":
-        rep = fbmoe_ep.TokenReplicator(T_EP)
-        full = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, device="cuda") for k in names if k != "routing_bias"}
-    w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
-    rows = T_EP // world
-    out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
-    main = torch.cuda.current_stream()
-    up, down = torch.cuda.Stream(), torch.cuda.Stream()
-    ev_in, ev_used, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
-    for i in range(2):
-        ev_used[i].record(main)
-        ev_out[i].record(main)
-    keys = ("up0", "up1", "c0", "gathered", "sent", "computed", "c1", "down0", "down1")
-    ev = [{k: torch.cuda.Event(enable_timing=True) for k in keys} for _ in range(steps + 2)]
-    host_ms = []
-    scale = inp["routed_scaling_factor"]
-
-    def one(i):
-        t0 = time.perf_counter()
-        b, x = i & 1, ev[i]
-        up.wait_event(ev_used[b])
-        with torch.cuda.stream(up):
-            x["up0"].record(up)
-            for k in names:
-                dev[b][k].copy_(host[k], non_blocking=True)
-            x["up1"].record(up)
-        ev_in[b].record(up)
-        main.wait_event(ev_in[b])
-        main.wait_event(ev_out[b])
-        x["c0"].record(main)
-        d = dev[b]
-        if rep is not None:
-            rep.gather(d["routing_logits"], d["hidden_states"], d["hidden_states_scale"], full["routing_logits"],
-                       full["hidden_states"], full["hidden_states_scale"])
-            d = dict(full, routing_bias=d["routing_bias"])
-        x["gathered"].record(main)
-        epoch = exchange._next_epoch()
-        if mode == "dispatch":
-            L.ep_dispatch_send(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"],
-                               T_EP, exchange.E_local, scale, rank, world, exchange.dispatch_ptrs, epoch,
-                               exchange.workspace)
-            x["sent"].record(main)
-            L.ep_dispatch_compute(*w, T_EP, rank, world, exchange.dispatch_local, exchange.ptrs, epoch,
-                                  exchange.workspace)
-        else:
-            x["sent"].record(main)
-            L.ep_send((d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"], *w,
-                       exchange.offset, scale), rank, world, exchange.ptrs, epoch, exchange.workspace, check=False)
-        x["computed"].record(main)
-        L.ep_recv(exchange.local, T_EP, rank, world, epoch, out_dev[b], exchange.workspace)
-        x["c1"].record(main)
-        ev_used[b].record(main)
-        down.wait_event(ev_used[b])
-        with torch.cuda.stream(down):
-            x["down0"].record(down)
-            out_host[b].copy_(out_dev[b], non_blocking=True)
-            x["down1"].record(down)
-        ev_out[b].record(down)
-        host_ms.append((time.perf_counter() - t0) * 1e3)
-
-    for i in range(2):
-        one(i)
-    torch.cuda.synchronize()
-    barrier(world)
-    host_ms.clear()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(main)
-    for i in range(2, steps + 2):
-        one(i)
-    main.wait_stream(down)
-    e.record(main)
-    torch.cuda.synchronize()
-    barrier(world)
-    tl = [{k: s.elapsed_time(v) for k, v in ev[i].items()} for i in range(2, steps + 2)]
-    med = lambda v: round(statistics.median(v), 3)  # noqa: E731
-    return {"rank": rank, "e2e_ms_per_step": round(s.elapsed_time(e) / steps, 3),
-            "upload": med([t["up1"] - t["up0"] for t in tl]),
-            "allgather": med([t["gathered"] - t["c0"] for t in tl]),
-            "dispatch_send": med([t["sent"] - t["gathered"] for t in tl]),
-            "experts_and_scatter": med([t["computed"] - t["sent"] for t in tl]),
-            "owner_combine": med([t["c1"] - t["computed"] for t in tl]),
-            "compute_step": med([t["c1"] - t["c0"] for t in tl]),
-            "download": med([t["down1"] - t["down0"] for t in tl]),
-            "gap_between_steps": med([tl[i]["c0"] - tl[i - 1]["c1"] for i in range(1, len(tl))]),
-            "host_enqueue": med(host_ms), "h2d_bytes": sum(v.numel() * v.element_size() for v in host.values()),
-            "status": exchange.status()}
-
-
 def run_ep_timeline(args):
     """--case ep-timeline under torchrun (N >= 2): device-only steps of both EP layers, host copy bandwidth per
-    rank alone and all ranks at once, and the per-step stream timelines of the e2e loops; one JSON line."""
+    rank alone and all ranks at once, and the per-step stream timelines of the e2e loops (run_e2e with events
+    on every stream of every step); one JSON line."""
     import torch.distributed as dist
     import fbmoe_ep
     world, rank, local = dist_setup()
@@ -845,10 +832,11 @@ def run_ep_timeline(args):
     dist.all_gather_object(objs, {"rank": rank, "alone": alone, "all_ranks_at_once": together})
     line["copy_gbs"] = objs
     for mode in ("dispatch", "replicated_full", "replicated_sliced"):
-        r = e2e_timeline(world, rank, inp, exchange, mode, steps=max(3, min(args.steps, 10)))
+        r = run_e2e(args, world, rank, inp, mode, exchange, instrument=True)
         objs = [None] * world
-        dist.all_gather_object(objs, r)
-        line["e2e_" + mode] = objs
+        dist.all_gather_object(objs, r["timeline"])
+        line["e2e_" + mode] = {"ms_per_step": r["ms_per_step"], "h2d_bytes_per_step": r["h2d_bytes_per_step"],
+                               "d2h_bytes_per_step": r["d2h_bytes_per_step"], "ranks": objs}
     exchange.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
