@@ -377,8 +377,9 @@ class E2ELoop:
         import fbmoe_lib as L
         self.L, self.world, self.rank, self.inp, self.exchange, self.mode = L, world, rank, inp, exchange, mode
         self.names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+        self.T = T = inp["routing_logits"].size(0)
         if mode in ("replicated_sliced", "dispatch"):
-            lo, hi = fbmoe_ep.row_range(rank, world, T_EP)
+            lo, hi = fbmoe_ep.row_range(rank, world, T)
             src = {"routing_logits": inp["routing_logits"][lo:hi], "routing_bias": inp["routing_bias"],
                    "hidden_states": inp["hidden_states"][lo:hi],
                    "hidden_states_scale": inp["hidden_states_scale"][:, lo:hi]}
@@ -388,18 +389,18 @@ class E2ELoop:
         self.dev = [{k: torch.empty(v.shape, dtype=v.dtype, device="cuda") for k, v in self.host.items()}
                     for _ in range(2)]
         self.w = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")]
-        rows = T_EP // world
+        rows = T // world
         self.out_host = [torch.empty((rows, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
         self.out_dev = [torch.empty((rows, H), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
         self.h2d = sum(v.numel() * v.element_size() for v in self.host.values())
         self.d2h = self.out_host[0].numel() * self.out_host[0].element_size()
         self.rep = self.full = None
         if mode == "replicated_sliced":
-            self.rep = fbmoe_ep.TokenReplicator(T_EP)
+            self.rep = fbmoe_ep.TokenReplicator(T)
             self.full = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, device="cuda")
                          for k in self.names if k != "routing_bias"}
         if mode == "nccl":
-            self.partial = torch.empty((T_EP, H), dtype=torch.float32, device="cuda")
+            self.partial = torch.empty((T, H), dtype=torch.float32, device="cuda")
             self.shard = torch.empty((rows, H), dtype=torch.float32, device="cuda")
         self.gate = mode in ("replicated_sliced", "dispatch")
         self.main = torch.cuda.current_stream()
@@ -445,7 +446,8 @@ class E2ELoop:
             d = dict(self.full, routing_bias=d["routing_bias"])
         if self.mode == "dispatch":
             L.ep_dispatch_send(d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"],
-                               T_EP, ex.E_local, scale, self.rank, self.world, ex.dispatch_ptrs, epoch, ex.workspace)
+                               self.T, ex.E_local, scale, self.rank, self.world, ex.dispatch_ptrs, epoch,
+                               ex.workspace)
         self.ev_x[b].record(main)
         _mark(marks, "exchanged", main)
         if self.pending is not None:
@@ -463,14 +465,14 @@ class E2ELoop:
             fbmoe_ep.combine(self.partial, out=self.out_dev[b], scratch=self.shard)
         else:
             if self.mode == "dispatch":
-                L.ep_dispatch_compute(*self.w, T_EP, self.rank, self.world, ex.dispatch_local, ex.ptrs, epoch,
+                L.ep_dispatch_compute(*self.w, self.T, self.rank, self.world, ex.dispatch_local, ex.ptrs, epoch,
                                       ex.workspace)
             else:
                 L.ep_send((d["routing_logits"], d["routing_bias"], d["hidden_states"], d["hidden_states_scale"],
                            *self.w, ex.offset, scale), self.rank, self.world, ex.ptrs, epoch, ex.workspace,
                           check=False)
             _mark(marks, "computed", main)
-            L.ep_recv(ex.local, T_EP, self.rank, self.world, epoch, self.out_dev[b], ex.workspace)
+            L.ep_recv(ex.local, self.T, self.rank, self.world, epoch, self.out_dev[b], ex.workspace)
         _mark(marks, "c1", main)
         self.ev_used[b].record(main)
         if self.gate:
@@ -517,7 +519,7 @@ def run_e2e(args, world, rank, inp, mode, exchange=None, steps=None, instrument=
     barrier(world)
     own = s.elapsed_time(e)
     ms = max_over_ranks(own, world)
-    res = {"value": round(T_EP * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": loop.h2d,
+    res = {"value": round(loop.T * n / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": loop.h2d,
            "d2h_bytes_per_step": loop.d2h, "steps": n, "ms_per_step": round(ms / n, 4), "mode": mode,
            "pipelining": "2 buffer sets; H2D and D2H on their own streams overlap the neighbouring steps' compute"
                          + ("; copies ordered after the step's NVLink exchange" if loop.gate else "")}

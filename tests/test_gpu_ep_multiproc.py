@@ -58,6 +58,22 @@ def _rank_main(rank, world, port, q):
             same = torch.equal(out.view(torch.int16), ref[lo:hi].view(torch.int16))
             if st != 0 or not same:
                 ok, msg = False, f"dispatch {config}: status {st}, equal {same}"
+        # bench.py's pipelined e2e loop on the token-dispatch layer: every downloaded row block equals the
+        # single-GPU operator's rows of this rank (copies ordered behind each step's dispatch send)
+        sys.path.insert(0, os.path.dirname(PKG))
+        import bench
+        shard = dict(inp, gemm1_weights=w1[off:off + E], gemm1_weights_scale=s1[off:off + E],
+                     gemm2_weights=w2[off:off + E], gemm2_weights_scale=s2[off:off + E], local_expert_offset=off)
+        loop = bench.E2ELoop(world, rank, shard, ex, "dispatch")
+        for i in range(4):
+            loop.step(i)
+        loop.flush()
+        torch.cuda.synchronize()
+        for b in range(2):
+            if not torch.equal(loop.out_host[b].view(torch.int16), ref[lo:hi].cpu().view(torch.int16)):
+                ok, msg = False, f"e2e loop slot {b} differs"
+        if ex.status() != 0:
+            ok, msg = False, f"e2e loop status {ex.status()}"
         ex.close()
         dist.destroy_process_group()
         q.put((rank, ok, msg))
