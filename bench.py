@@ -543,15 +543,15 @@ def run_e2e(args, world, rank, inp, mode, exchange=None, steps=None, instrument=
 def launches_per_forward(T, E_local, world=1, p2p=False):
     """Our kernels per forward (mirrors forward_core in csrc/moe_capi.cu): T <= 16: router+permute (one CTA),
     decode kernel; T <= 64: router, permute, decode kernel; otherwise router, [per-chunk count], permute, gather,
-    GEMM1, GEMM2, combine.  The peer-memory
-    expert-parallel path (csrc/moe_ep.cu) always takes the second chain and replaces the combine with a
-    flag-release kernel and the owner's combine."""
+    GEMM1, GEMM2 (two launches: the pairs kernel and the one-block kernel, one of which returns at once), combine.
+    The peer-memory expert-parallel path (csrc/moe_ep.cu) always takes the second chain and replaces the combine
+    with a flag-release kernel and the owner's combine."""
     import fbmoe_lib as L
     if p2p and world > 1:
-        return 7 + (1 if T > 1024 else 0)
+        return 8 + (1 if T > 1024 else 0)
     if L.block_rows(T, E_local) == 16:
         return 2 if T <= 16 else 3
-    return 6 + (1 if T > 1024 else 0)
+    return 7 + (1 if T > 1024 else 0)
 
 
 def flush_l2(buf):

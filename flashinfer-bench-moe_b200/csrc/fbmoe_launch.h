@@ -181,7 +181,11 @@ cudaError_t launch_gemm2_fp8_rows(const CUtensorMap* tm_w2, const CUtensorMap* t
                                   int num_sms, cudaStream_t stream, const PeerScatter* scatter = nullptr);
 
 // GEMM2 for blocks of 128 rows with the tokens as the MMA M operand; tm_w2raw
-// maps W2 as unswizzled 64-byte x 256-row boxes.
+// maps W2 as unswizzled 64-byte x 256-row boxes.  Launches the pairs kernel and
+// the one-block kernel; the device picks which of them does the work.
+cudaError_t launch_gemm2_pairs(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
+                               const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream,
+                               const PeerScatter* scatter = nullptr);
 cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
                               const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream,
                               const PeerScatter* scatter = nullptr);

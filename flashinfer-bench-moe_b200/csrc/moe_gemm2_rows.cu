@@ -1,6 +1,9 @@
 // moe_gemm2_rows.cu -- GEMM2 x routing weight for large token blocks (prefill),
 // tokens as the MMA's M operand (tcgen05 kind::f16, TMEM, TMA), sm_100a.
 //
+// One row block per unit; calls whose experts have many blocks run the pairs kernel
+// instead (moe_gemm2_pairs.cu, chosen on the device: gemm2_pairs_mode).
+//
 // Counterpart of the reference's gemm2_kernel (solution/triton/main.py:433-600),
 // and the same arithmetic as the GEMM2 phase of moe_decode.cu:
 //     pair_out[r, h] = w[r] * sum_j inter[r, j] * W2[e, h, j] * s2[e, h/128, j/128].
@@ -88,7 +91,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const int4* __restrict__ blocks, const float* __restrict__ row_weight,
                       __half* __restrict__ pair_out, uint32_t* __restrict__ status,
                       const int32_t* __restrict__ row_token, const int32_t* __restrict__ token_rows,
-                      const PeerScatter ps, int T, int e_local, int pcap) {
+                      const PeerScatter ps, int T, int e_local, int pcap,
+                      const int32_t* __restrict__ expert_cnt) {
+  // The pairs kernel (launched just before) takes calls whose experts have many blocks.
+  {
+    __shared__ int red[16];
+    __shared__ int s_pairs;
+    if (threadIdx.x < 256) {
+      const bool pm = gemm2_pairs_mode(expert_cnt, e_local, *n_blocks_ptr, red);
+      if (threadIdx.x == 0) s_pairs = pm ? 1 : 0;
+    }
+    __syncthreads();
+    if (s_pairs) {
+      pdl_trigger();
+      pdl_wait();  // complete only after the grids before it (the reduce relies on it)
+      return;
+    }
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sRaw = sm + kOffRaw;
@@ -386,6 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm_inter, const float* w2_scale,
                               const Layout& L, uint8_t* ws, int num_sms, cudaStream_t stream,
                               const PeerScatter* scatter) {
+  // both kernels; the one the routing does not choose returns after its grid dependency
+  if (cudaError_t err = launch_gemm2_pairs(tm_w2raw, tm_inter, w2_scale, L, ws, num_sms, stream, scatter);
+      err != cudaSuccess)
+    return err;
   static DeviceFlags attr_set;
   if (cudaError_t err = set_max_dynamic_smem(gemm2_rows_kernel, kSmemBytes, attr_set); err != cudaSuccess) return err;
   PeerScatter ps{};
@@ -397,7 +420,8 @@ cudaError_t launch_gemm2_rows(const CUtensorMap* tm_w2raw, const CUtensorMap* tm
                     reinterpret_cast<const int32_t*>(ws + L.n_blocks), reinterpret_cast<const int4*>(ws + L.blocks),
                     reinterpret_cast<const float*>(ws + L.row_weight), reinterpret_cast<__half*>(ws + L.pair_out),
                     reinterpret_cast<uint32_t*>(ws + L.status), reinterpret_cast<const int32_t*>(ws + L.row_token),
-                    reinterpret_cast<const int32_t*>(ws + L.token_rows), ps, L.tokens, L.e_local, L.pcap);
+                    reinterpret_cast<const int32_t*>(ws + L.token_rows), ps, L.tokens, L.e_local, L.pcap,
+                    reinterpret_cast<const int32_t*>(ws + L.expert_cnt));
 }
 
 }  // namespace fbmoe
