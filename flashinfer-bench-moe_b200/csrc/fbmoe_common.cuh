@@ -430,10 +430,11 @@ __device__ __forceinline__ uint64_t f32x2_mul(uint64_t a, uint64_t b) {
 // Prefill GEMM2 runs as one of two kernels chosen on the device from the routing:
 // both are launched, one after the other, and the one not chosen only waits for
 // its grid dependency and returns.  Experts' 128-row blocks are worked in pairs
-// (moe_gemm2_pairs.cu) when the blocks number at least 3 per active expert
-// (measured: 13-15 % faster GEMM2 under skewed routing, 0-4 % slower at about 2
-// blocks per expert, where one block per unit keeps the accumulators
-// double-buffered, moe_gemm2_rows.cu).  A block list the permutation cut short
+// (moe_gemm2_pairs.cu) when the blocks number at least 2 per active expert
+// (measured: 13-15 % faster GEMM2 under skewed routing, 3.5 % faster per call at
+// config 3's 2.96 blocks per expert); with about one block per expert, units stay
+// single and one block per unit keeps the accumulators double-buffered
+// (moe_gemm2_rows.cu).  A block list the permutation cut short
 // goes to the one-block kernel.  Run by threads 0..255 of the CTA (named barrier
 // 1); every one of them gets the same answer.  red: 16 ints of shared memory.
 __device__ __forceinline__ bool gemm2_pairs_mode(const int32_t* __restrict__ expert_cnt, int e_local, int nb_all,
@@ -453,7 +454,7 @@ __device__ __forceinline__ bool gemm2_pairs_mode(const int32_t* __restrict__ exp
     tot_nb += red[w];
     tot_act += red[8 + w];
   }
-  return tot_nb == nb_all && tot_act > 0 && tot_nb >= 3 * tot_act;
+  return tot_nb == nb_all && tot_act > 0 && tot_nb >= 2 * tot_act;
 }
 
 // ------------------------------------------- 1x128 e4m3 quantisation -------

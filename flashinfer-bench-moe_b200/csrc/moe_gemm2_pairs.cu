@@ -1,7 +1,7 @@
 // moe_gemm2_pairs.cu -- GEMM2 x routing weight for large token blocks (prefill),
 // tokens as the MMA's M operand (tcgen05 kind::f16, TMEM, TMA), sm_100a.
 //
-// Runs the calls whose experts have many 128-row blocks (at least 3 per active
+// Runs the calls whose experts have several 128-row blocks (at least 2 per active
 // expert, gemm2_pairs_mode); other calls run moe_gemm2_rows.cu, which is launched
 // right after this kernel.
 //
