@@ -16,7 +16,7 @@ At N > 1 the line's `token_dispatch` object (inputs token-sharded: each rank hol
 T/N tokens) carries its own `e2e`, in which each rank uploads only its tokens.
 On N = 1 the line also carries the decode sweep (config 1: T = 1..64, 32 local
 experts, HBM roofline) and prefill points (config 2: skewed routing, FP8 tensor
-roofline), each measured with L2 flushed between calls, after a 5 s idle pause
+roofline), each measured with L2 flushed (cold and clean, L2Flush) between calls, after a 5 s idle pause
 that lets the SM clock recover from the power-capped config-3 loop, and each with
 its own `clocks` record.
 
@@ -554,8 +554,23 @@ def launches_per_forward(T, E_local, world=1, p2p=False):
     return 7 + (1 if T > 1024 else 0)
 
 
-def flush_l2(buf):
-    buf.add_(1)  # 256 MB read+write > 126 MB L2
+class L2Flush:
+    """Called between timed calls.  A 256 MB read-modify-write evicts everything the previous call left in the
+    126 MB L2.  In the default "clean" mode a read of another 256 MB follows, so the write's own dirty lines go
+    back to DRAM before the timed call starts (a cold, clean L2: the state ncu's cache control gives a profiled
+    launch).  "dirty" skips that read: the timed call then starts by writing back up to ~126 MB of the flush's
+    data, which a streaming kernel pays for in DRAM time as if it were its own traffic."""
+
+    def __init__(self, mode="clean"):
+        assert mode in ("clean", "dirty")
+        self.mode = mode
+        self.w = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+        self.r = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device="cuda") if mode == "clean" else None
+
+    def __call__(self):
+        self.w.add_(1)
+        if self.r is not None:
+            torch.amax(self.r)
 
 
 def time_calls(fn, iters, flush):
@@ -577,25 +592,29 @@ def decode_sweep(peaks):
     import fbmoe_lib as L
     import fbmoe_workloads as W
     weights = W.make_weights(32, 4242, "cuda")
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    flush, dirty = L2Flush(), L2Flush("dirty")
     res = []
     for T in (1, 2, 4, 8, 16, 32, 64):
         inp = W.make_inputs(T, seed=T, config="standard", device="cuda", weights=weights)
         args = W.as_args(inp)
-        us = 1e3 * time_calls(lambda: L.forward(*args, check=False), 30, lambda: flush_l2(buf))
+        us = 1e3 * time_calls(lambda: L.forward(*args, check=False), 30, flush)
+        us_dirty = 1e3 * time_calls(lambda: L.forward(*args, check=False), 30, dirty)
         # stage breakdown from a separate pass: the events between stages serialise the launches
         L.profile_begin(8)
-        time_calls(lambda: L.forward(*args, check=False), 5, lambda: flush_l2(buf))
+        time_calls(lambda: L.forward(*args, check=False), 5, flush)
         stage_ms, nf = L.profile_end()
         pairs, active = local_pairs(inp, 32, 0)
         nbytes = active * BYTES_PER_EXPERT + BYTES_PER_TOKEN * T + 512
         gbs = nbytes / (us / 1e6) / 1e9
         res.append({"T": T, "us_per_call": round(us, 2), "active_experts": active, "local_pairs": pairs,
                     "algorithmic_bytes": nbytes, "hbm_gbs": round(gbs, 1),
-                    "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                    "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "us_per_call_dirty_l2": round(us_dirty, 2),
+                    "frac_hbm_dirty_l2": round(nbytes / (us_dirty / 1e6) / 1e9 / peaks["hbm_gbs"], 4),
                     "stage_us_profiled": {n: round(1e3 * stage_ms[i] / max(nf, 1), 1) for i, n in enumerate(L.STAGES)}})
     del weights
+    del dirty
     return {"config": "config1 decode, 32 local experts, offset 0, L2 flushed between calls",
+            "flush": "clean (L2Flush); *_dirty_l2: the same calls after a flush that leaves its dirty lines in L2",
             "peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"], "points": res}
 
 
@@ -604,24 +623,26 @@ def quantiser_point(peaks, T=8192):
     HBM roofline: 14,336 B read + 7,168 + 224 B written per token."""
     import fbmoe_lib as L
     x = (torch.randn((T, H), device="cuda") * 3).to(torch.bfloat16)
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
-    ms = time_calls(lambda: L.quantize_act(x), 20, lambda: flush_l2(buf))
+    flush, dirty = L2Flush(), L2Flush("dirty")
+    ms = time_calls(lambda: L.quantize_act(x), 20, flush)
+    ms_dirty = time_calls(lambda: L.quantize_act(x), 20, dirty)
     nbytes = T * (2 * H + H + 4 * (H // 128))
     gbs = nbytes / (ms / 1e3) / 1e9
     return {"T": T, "us_per_call": round(ms * 1e3, 2), "algorithmic_bytes": nbytes, "hbm_gbs": round(gbs, 1),
-            "frac_hbm": round(gbs / peaks["hbm_gbs"], 4)}
+            "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "us_per_call_dirty_l2": round(ms_dirty * 1e3, 2),
+            "frac_hbm_dirty_l2": round(nbytes / ms_dirty / 1e6 / peaks["hbm_gbs"], 4)}
 
 
 def prefill_points(peaks):
     import fbmoe_lib as L
     import fbmoe_workloads as W
     weights = W.make_weights(32, 4242, "cuda")
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    flush = L2Flush()
     res = []
     for T in (1024, 4096, 8192):
         inp = W.make_inputs(T, seed=T, config="skew", device="cuda", weights=weights)
         args = W.as_args(inp)
-        ms = time_calls(lambda: L.forward(*args, check=False), 10, lambda: flush_l2(buf))
+        ms = time_calls(lambda: L.forward(*args, check=False), 10, flush)
         pairs, active = local_pairs(inp, 32, 0)
         flops = pairs * FLOPS_PER_PAIR
         tf = flops / (ms / 1e3) / 1e12
@@ -642,7 +663,7 @@ def prepack_points(peaks):
     import fbmoe_workloads as W
     weights = W.make_weights(32, 4242, "cuda")
     packed = L.prepack_w1(weights[0])
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    flush = L2Flush()
     res = []
     for T, cfg, iters in ((1, "standard", 30), (8, "standard", 30), (64, "standard", 30), (4096, "skew", 10),
                           (8192, "skew", 10)):
@@ -650,8 +671,8 @@ def prepack_points(peaks):
         raw_args = W.as_args(inp)
         pk_args = list(raw_args)
         pk_args[4] = packed
-        raw = time_calls(lambda: L.forward(*raw_args, check=False), iters, lambda: flush_l2(buf))
-        pk = time_calls(lambda: L.forward(*pk_args, check=False, w1_packed=True), iters, lambda: flush_l2(buf))
+        raw = time_calls(lambda: L.forward(*raw_args, check=False), iters, flush)
+        pk = time_calls(lambda: L.forward(*pk_args, check=False, w1_packed=True), iters, flush)
         res.append({"T": T, "config": cfg, "raw_us": round(raw * 1e3, 2), "prepacked_us": round(pk * 1e3, 2),
                     "speedup": round(raw / pk, 4)})
     del packed, weights
@@ -666,14 +687,14 @@ def fp8_intermediate_points(peaks, inp_ep):
     import fbmoe_lib as L
     import fbmoe_workloads as W
     weights = W.make_weights(32, 4242, "cuda")
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    flush = L2Flush()
     cases = [(T, "config2_skew", W.as_args(W.make_inputs(T, seed=T, config="skew", device="cuda", weights=weights)))
              for T in (4096, 8192)]
     cases.append((T_EP, "config3_ep1", W.as_args(inp_ep)))
     res = []
     for T, name, args in cases:
-        f16 = time_calls(lambda: L.forward(*args, check=False), 6, lambda: flush_l2(buf))
-        fp8 = time_calls(lambda: L.forward(*args, check=False, intermediate="fp8"), 6, lambda: flush_l2(buf))
+        f16 = time_calls(lambda: L.forward(*args, check=False), 6, flush)
+        fp8 = time_calls(lambda: L.forward(*args, check=False, intermediate="fp8"), 6, flush)
         E = args[4].size(0)
         idx, _ = L.route(args[0], args[1], args[9])
         pairs = int(((idx >= args[8]) & (idx < args[8] + E)).sum().item())
@@ -857,12 +878,12 @@ def run_case(args):
     inp = W.make_inputs(args.T, seed=args.T, config="skew" if args.case == "prefill" else "standard",
                         device="cuda", weights=weights)
     fargs = W.as_args(inp)
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    flush = L2Flush()
     for _ in range(args.warmup):
         L.forward(*fargs, check=False)
     ts = []
     for _ in range(args.steps):
-        flush_l2(buf)
+        flush()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         L.forward(*fargs, check=False)
