@@ -869,11 +869,23 @@ def run_ep_timeline(args):
 
 def run_case(args):
     """One config at one T on GPU 0 (used for profiling captures): decode = config 1,
-    prefill = config 2 (skewed routing); 32 local experts, L2 flushed between calls."""
+    prefill = config 2 (skewed routing); 32 local experts, L2 flushed between calls.
+    quant = the activation quantiser alone on T rows."""
     import fbmoe_lib as L
     import fbmoe_workloads as W
     torch.cuda.set_device(0)
     peaks = load_peaks()
+    if args.case == "quant":
+        x = (torch.randn((args.T, H), device="cuda") * 3).to(torch.bfloat16)
+        flush = L2Flush()
+        for _ in range(args.warmup):
+            L.quantize_act(x)
+        ms = time_calls(lambda: L.quantize_act(x), args.steps, flush)
+        nbytes = args.T * (2 * H + H + 4 * (H // 128))
+        print(json.dumps({"case": "quant", "T": args.T, "us_per_call": round(ms * 1e3, 2),
+                          "hbm_gbs": round(nbytes / (ms / 1e3) / 1e9, 1), "peak_hbm_gbs": peaks["hbm_gbs"]}),
+              flush=True)
+        return
     weights = W.make_weights(32, 4242, "cuda")
     inp = W.make_inputs(args.T, seed=args.T, config="skew" if args.case == "prefill" else "standard",
                         device="cuda", weights=weights)
@@ -910,12 +922,13 @@ def main():
                          "NCCL reduce-scatter (nccl)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode/prefill sweeps (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--case", choices=("ep", "decode", "prefill", "shard", "ep-timeline"), default="ep",
-                    help="ep = the benchmark line (default); decode/prefill/shard = one small config for profiling "
-                         "(shard = uniform routing over 32 local experts: one rank's work at N=8 when T=8192); "
+    ap.add_argument("--case", choices=("ep", "decode", "prefill", "shard", "quant", "ep-timeline"), default="ep",
+                    help="ep = the benchmark line (default); decode/prefill/shard/quant = one small config for "
+                         "profiling (quant = the activation quantiser on T rows; "
+                         "shard = uniform routing over 32 local experts: one rank's work at N=8 when T=8192); "
                          "ep-timeline = per-rank stream timelines of the e2e loops and host copy bandwidth "
                          "(torchrun, N >= 2)")
-    ap.add_argument("--T", type=int, default=64, help="tokens for --case decode/prefill")
+    ap.add_argument("--T", type=int, default=64, help="tokens for --case decode/prefill/shard/quant")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

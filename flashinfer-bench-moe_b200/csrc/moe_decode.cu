@@ -135,7 +135,8 @@ static_assert(kP2Planes % 1024 == 0, "the planes are 128-byte swizzle atoms");
 struct DecodeArgs {
   CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
   CUtensorMap tm_w2;     // W2 rows x 2048 K, 128-byte x 128-row boxes
-  CUtensorMap tm_planes;  // GEMM2 B planes: [2 * pcap rows] x 2048 fp8, 128-byte x 16-row boxes
+  // GEMM2 B planes: [2 * pcap rows] x 2048 fp8, 128-byte boxes of 1, 2, 4, 8 and 16 rows
+  CUtensorMap tm_planes[kPlaneBoxes];
   CUtensorMap tm_pscale;  // their scales: [2 * 32 chunk rows] x pcap fp32, 16 x 32 boxes
   const uint8_t* hidden;
   const float* hidden_scale;
@@ -181,10 +182,27 @@ struct Ring {
   }
 };
 
-__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+__device__ __forceinline__ int ld_relaxed_gpu(const int32_t* p) {
   int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void red_release_gpu_add(int32_t* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until *p >= target (a counter raised by release-adds of other CTAs), then
+// acquire: relaxed polling (no sleep: the counter is one L2 line and one thread per
+// CTA polls it) and one acquire fence once the target is seen.  Returns false when
+// `abort` is raised or the wall-time budget runs out.
+__device__ __forceinline__ bool wait_counter(const int32_t* p, int target, volatile int* abort, uint64_t budget_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1; ld_relaxed_gpu(p) < target; ++it) {
+    if ((it & 31u) == 0 && (*abort || globaltimer_ns() - t0 > budget_ns)) return false;
+  }
+  fence_acq_rel_gpu();
+  return true;
 }
 
 // Balanced partition of one phase's K-blocks over the CTAs that take part
@@ -230,6 +248,7 @@ __device__ __forceinline__ Seg seg_at(const Partition& P, int x, int end) {
 // Phase partitions.  Stream-K: GEMM1 ranges hold >= 8 K-blocks (a unit has up to 8
 // segments; a CTA writes at most 2 partials: its first and its last unit); GEMM2
 // ranges hold >= 16 K-blocks = one unit, so a unit has at most 2 segments = planes.
+constexpr int kSegBatch = 4;  // fix-up: segment partials loaded per L2 round trip
 __device__ __forceinline__ Partition gemm1_partition(int nb, bool streamk) {
   const int units = nb * kG1Slices, total = units * kHBlocks;
   const int g = streamk ? max(1, min((int)gridDim.x, total / 8)) : max(1, min((int)gridDim.x, units));
@@ -495,24 +514,44 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
         const int r = 2 * lane;
         float y[2] = {0.0f, 0.0f};
         if (t < nrows) {
+          float x1[2] = {0.0f, 0.0f}, x2[2] = {0.0f, 0.0f};
+          if (nseg == 1) {
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            float x1 = 0.0f, x2 = 0.0f;
-            if (nseg == 1) {
+            for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
               for (int j = 0; j < G; ++j) {
-                x1 += sXch[(size_t)(j * 128 + r + cc) * kXchStride + t];
-                x2 += sXch[(size_t)(j * 128 + 64 + r + cc) * kXchStride + t];
+                x1[cc] += sXch[(size_t)(j * 128 + r + cc) * kXchStride + t];
+                x2[cc] += sXch[(size_t)(j * 128 + 64 + r + cc) * kXchStride + t];
               }
-            } else {
-              for (int q = 0; q < nseg; ++q) {  // segment order: deterministic
-                const float* pq = a.split_part + (size_t)partial_slot(P, c0 + q, u) * 128 * BN;
-                x1 += __ldcg(pq + (r + cc) * BN + t);
-                x2 += __ldcg(pq + (64 + r + cc) * BN + t);
+          } else {
+            // the partials of up to four segments are loaded before any is added (one
+            // L2 round trip per four segments, not per segment), then summed in
+            // segment order (deterministic)
+            for (int q0 = 0; q0 < nseg; q0 += kSegBatch) {
+              float p1[kSegBatch][2], p2[kSegBatch][2];
+#pragma unroll
+              for (int q = 0; q < kSegBatch; ++q) {
+                if (q0 + q < nseg) {
+                  const float* pq = a.split_part + (size_t)partial_slot(P, c0 + q0 + q, u) * 128 * BN;
+#pragma unroll
+                  for (int cc = 0; cc < 2; ++cc) {
+                    p1[q][cc] = __ldcg(pq + (r + cc) * BN + t);
+                    p2[q][cc] = __ldcg(pq + (64 + r + cc) * BN + t);
+                  }
+                }
               }
+#pragma unroll
+              for (int q = 0; q < kSegBatch; ++q)
+                if (q0 + q < nseg)
+#pragma unroll
+                  for (int cc = 0; cc < 2; ++cc) {
+                    x1[cc] += p1[q][cc];
+                    x2[cc] += p2[q][cc];
+                  }
             }
-            y[cc] = x2 / (1.0f + expf(-x2)) * x1;
           }
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) y[cc] = x2[cc] / (1.0f + expf(-x2[cc])) * x1[cc];
         }
         if (!isfinite(y[0]) || !isfinite(y[1])) {
           atomicOr(a.status, kStatusSaturated);
@@ -546,7 +585,7 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
       }
       named_barrier_sync(1, kEpi1Threads);
       // one more of this block's 32 slices is published (GEMM2 waits for all 32)
-      if (last && etid == 0) atomicAdd(&a.blk_ready[u / kG1Slices], 1);
+      if (last && etid == 0) red_release_gpu_add(&a.blk_ready[u / kG1Slices], 1);
     }
   }
 }
@@ -640,24 +679,26 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
           break;
         }
         // GEMM1 published all 32 slices of the block's rows
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_gpu(&a.blk_ready[b]) < kG1Slices) {
-          if (*sAbort || globaltimer_ns() - t0 > kWaitBudgetNs) {
-            ok = false;
-            fail(kStatusTimeoutProducer);
-            break;
-          }
-          __nanosleep(100);
+        if (!wait_counter(&a.blk_ready[b], kG1Slices, sAbort, kWaitBudgetNs)) {
+          ok = false;
+          fail(kStatusTimeoutProducer);
+          break;
         }
-        if (!ok) break;
         fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
-        const int r0 = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status).y;
-        mbar_arrive_expect_tx(planes_full, kIBlocks * kPlaneKBytes + 2 * BN * kChunks * 4);
+        const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
+        const int r0 = blk.y;
+        // Only the first R = 2^lg >= nrows rows of each plane tile: the MMA's columns
+        // for rows R..15 read stale shared memory, and their results are never used
+        // (pair rows are stored for t < nrows only).  At decode sizes a block holds a
+        // few rows, so this cuts the CTA's planes load from 64 KB to 4-16 KB.
+        const int lg = blk.z <= 1 ? 0 : blk.z <= 2 ? 1 : blk.z <= 4 ? 2 : blk.z <= 8 ? 3 : 4;
+        const CUtensorMap* tmp = &a.tm_planes[lg];
+        mbar_arrive_expect_tx(planes_full, kIBlocks * 2 * (128u << lg) + 2 * BN * kChunks * 4);
         for (int kb = 0; kb < kIBlocks; ++kb)
 #pragma unroll
           for (int pl = 0; pl < 2; ++pl)
-            tma_load_2d(sPlanes + kb * kPlaneKBytes + pl * BN * 128, &a.tm_planes, planes_full, kb * kBlk,
-                        pl * a.pcap + r0, pol);
+            tma_load_2d(sPlanes + kb * kPlaneKBytes + pl * BN * 128, tmp, planes_full, kb * kBlk, pl * a.pcap + r0,
+                        pol);
 #pragma unroll
         for (int pl = 0; pl < 2; ++pl)
           tma_load_2d(sm + kP2PScale + pl * BN * kChunks * 4, &a.tm_pscale, planes_full, r0, pl * kChunks, pol);
@@ -826,21 +867,15 @@ __device__ __forceinline__ void combine_phase(const DecodeArgs& a, int nb, volat
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) np[k] = rows[k] >= 0 ? P2.nseg((rows[k] / BN) * kG2Slices + h) : 0;
   };
-  if (threadIdx.x == 0) {
-    __threadfence();  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
-    atomicAdd(a.grid_sync, 1);
-  }
+  // this CTA's pair rows (ordered before by the CTA barrier) are visible grid-wide
+  // once the release-add lands
+  if (threadIdx.x == 0) red_release_gpu_add(a.grid_sync, 1);
   // the first task's slot rows load while the other CTAs arrive
   if (first < tasks) prep(first);
   if (threadIdx.x == 0) {
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_gpu(a.grid_sync) < (int)gridDim.x + a.grid_extra) {
-      if (globaltimer_ns() - t0 > a.grid_wait_ns) {
-        *sAbort = 1;
-        atomicOr(a.status, kStatusTimeoutEpilogue);
-        break;
-      }
-      __nanosleep(100);
+    if (!wait_counter(a.grid_sync, (int)gridDim.x + a.grid_extra, sAbort, a.grid_wait_ns)) {
+      *sAbort = 1;
+      atomicOr(a.status, kStatusTimeoutEpilogue);
     }
   }
   __syncthreads();
@@ -933,7 +968,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&a.tm_w1);
     tma_prefetch_desc(&a.tm_w2);
-    tma_prefetch_desc(&a.tm_planes);
+    for (int i = 0; i < kPlaneBoxes; ++i) tma_prefetch_desc(&a.tm_planes[i]);
     tma_prefetch_desc(&a.tm_pscale);
   }
   if (warp == 1) {
@@ -997,7 +1032,7 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   DecodeArgs a;
   a.tm_w1 = *tm_w1;
   a.tm_w2 = *tm_w2;
-  a.tm_planes = *tm_planes;
+  for (int i = 0; i < kPlaneBoxes; ++i) a.tm_planes[i] = tm_planes[i];
   a.tm_pscale = *tm_pscale;
   a.hidden = hidden;
   a.hidden_scale = hidden_scale;
