@@ -139,11 +139,8 @@ cudaError_t launch_permute(const int32_t* topk_idx, const float* topk_w, int T, 
 // Decode (16-row blocks): GEMM1 + SwiGLU, GEMM2 x routing weight and the
 // per-token combine in one persistent kernel; writes out (bf16, or fp32 partial
 // sums with f32_out).
-// tm_planes: kPlaneBoxes maps of the intermediate planes, box heights 1, 2, 4, 8, 16 rows.
 // sink: host-visible status sink of the workspace (nullptr: none).
-constexpr int kPlaneBoxes = 5;
-cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_planes,
-                          const CUtensorMap* tm_pscale,
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
                           uint32_t* sink, bool w1_packed, cudaStream_t stream);

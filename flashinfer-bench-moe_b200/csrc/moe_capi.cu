@@ -260,20 +260,9 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   rc = encode_2d(&tm_w2raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gemm2_weights, kInter, (uint64_t)E_local * kHidden, 64,
                  256, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  CUtensorMap tm_planes[kPlaneBoxes], tm_pscale;
-  if (bn == 16) {
-    // decode: GEMM1 writes the intermediate as two fp8 planes [2][pcap][2048] (in the
-    // f16 intermediate's region) with scales [2][32][pcap]; GEMM2 loads the first
-    // 1, 2, 4, 8 or 16 rows of a block (the power of two that covers its rows)
-    for (int i = 0; i < kPlaneBoxes; ++i) {
-      rc = encode_2d(&tm_planes[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + L.inter, kInter, 2 * (uint64_t)L.pcap,
-                     128, 1u << i);
-      if (rc) return rc;
-    }
-    rc = encode_2d(&tm_pscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws + L.plane_scale, (uint64_t)L.pcap,
-                   2 * (kInter / 64), 16, kInter / 64, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  } else {
+  // decode (bn == 16) keeps the intermediate as two fp8 planes that its GEMM2 copies
+  // with cp.async (no tensor map); prefill GEMM2 loads the f16 intermediate by TMA
+  if (bn != 16) {
     rc = encode_2d(&tm_inter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws + L.inter, kInter, (uint64_t)L.pcap, 64,
                    (uint32_t)bn);
     if (rc) return rc;
@@ -323,7 +312,7 @@ int forward_core(const float* routing_logits, const void* routing_bias, const vo
   if (bn == 16) {
     // decode: GEMM1, GEMM2 and the combine run as one kernel (its time is the
     // "gemm1" stage of the profile; "gemm2" and "combine" stay empty)
-    e = launch_decode(&tm_w1, &tm_w2, tm_planes, &tm_pscale, reinterpret_cast<const uint8_t*>(hidden_states),
+    e = launch_decode(&tm_w1, &tm_w2, reinterpret_cast<const uint8_t*>(hidden_states),
                       hidden_states_scale,
                       T, gemm1_weights_scale, gemm2_weights_scale, L, ws, out, f32_out, sms, sink, w1_packed,
                       stream);

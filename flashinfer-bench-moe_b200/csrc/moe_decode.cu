@@ -48,15 +48,15 @@
 //
 // GEMM2 phase.  Work unit = (block) x (slice h of 128 hidden columns): A = 128
 // raw fp8 W2 rows (TMA ring), exact; B = the block's two intermediate planes
-// (2 x 16 rows, fp8, TMA), resident in shared memory for the CTA's units of that
-// block.  Per K-block one kind::f8f6f4 MMA per 64-K chunk (N = 32: both planes)
+// (2 x 16 rows, fp8, the block's rows copied with cp.async), resident in shared
+// memory for the CTA's units of that block.  Per K-block one kind::f8f6f4 MMA per 64-K chunk (N = 32: both planes)
 // into one of 8 TMEM slots, one commit per K-block; promotion warps add
 // D * s2 * plane_scale in fp32 registers per chunk and plane.  Stream-K as in
 // GEMM1, with ranges of >= 16 K-blocks, so a unit has at most two segments;
 // segment s writes plane s of the pair rows and the combine adds a unit's planes.
 // Warps: w0 W2 producer (TMA), w1 MMA issuer, w2 planes producer (waits for the
-// block's GEMM1 slices, then TMA), w3 idle, w4-w19 promotion; then all threads
-// combine.
+// block's GEMM1 slices, then cp.async), w3 idle, w4-w19 promotion; then all
+// threads combine.
 #include <cstdlib>
 
 #include "fbmoe_common.cuh"
@@ -135,9 +135,6 @@ static_assert(kP2Planes % 1024 == 0, "the planes are 128-byte swizzle atoms");
 struct DecodeArgs {
   CUtensorMap tm_w1;     // W1 rows x 7168 K, 128-byte x 64-row boxes
   CUtensorMap tm_w2;     // W2 rows x 2048 K, 128-byte x 128-row boxes
-  // GEMM2 B planes: [2 * pcap rows] x 2048 fp8, 128-byte boxes of 1, 2, 4, 8 and 16 rows
-  CUtensorMap tm_planes[kPlaneBoxes];
-  CUtensorMap tm_pscale;  // their scales: [2 * 32 chunk rows] x pcap fp32, 16 x 32 boxes
   const uint8_t* hidden;
   const float* hidden_scale;
   const float* w1_scale;
@@ -604,8 +601,8 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
 // within 0.13x the output tolerance (0.08x for the f16 intermediate with f16 W2 this
 // replaces, 0.40x for bf16, 5.8x for a single fp8 plane).
 //
-// Warps: w0 W2 producer (TMA ring); w2 loads a block's planes and scales (TMA,
-// once per block, after GEMM1 published the block's 32 slices and the MMAs on the
+// Warps: w0 W2 producer (TMA ring); w2 copies a block's planes and scales (cp.async
+// by the whole warp, once per block, after GEMM1 published the block's 32 slices and the MMAs on the
 // previous block's planes completed); w1 MMA issuer; w4-w19 promote every chunk,
 // each warp four token rows of its TMEM lane quarter, and at a unit's end multiply
 // by the routing weights and store the f16 pair rows of the segment's plane.
@@ -617,7 +614,7 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
   const float* sPScale = reinterpret_cast<const float*>(sm + kP2PScale);  // [2 planes][32 chunks][16 rows]
   uint64_t* raw_full = bars;                  // W2 tile landed (TMA)
   uint64_t* raw_empty = bars + SR;            // MMA done with it (a promotion thread, after the slot's commit)
-  uint64_t* planes_full = bars + 2 * SR;      // a block's planes and scales landed (TMA)
+  uint64_t* planes_full = bars + 2 * SR;      // a block's planes and scales copied (cp.async, one arrive)
   uint64_t* planes_empty = planes_full + 1;   // MMA done with them (another block follows)
   uint64_t* tfull = planes_full + 2;
   uint64_t* tempty = tfull + kSlots2;
@@ -664,8 +661,12 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
     __syncwarp();
   } else if (warp == 2) {
     // ------------------------------------------------------------ planes producer
-    if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_last();
+    // The whole warp copies a block's planes and their scales with cp.async (generic
+    // proxy: it reads what other CTAs stored after the counter's acquire without a
+    // global proxy fence), then one shared-memory proxy fence hands them to the MMA.
+    // Only the block's rows of the planes are copied: the MMA's columns for the other
+    // rows read stale shared memory and their results are never stored.
+    {
       int cur_blk = -1, nblk = 0;
       bool ok = true;
       for (int x = x_beg; x < x_end && ok;) {
@@ -675,38 +676,40 @@ __device__ __forceinline__ void gemm2_phase(const DecodeArgs& a, uint8_t* sm, ui
         if (b == cur_blk) continue;
         // the MMAs on the previous block's planes have completed
         if (nblk > 0 && !mbar_wait(planes_empty, (uint32_t)(nblk - 1) & 1u, sAbort, kWaitBudgetNs)) {
-          fail(kStatusTimeoutProducer);
+          if (lane == 0) fail(kStatusTimeoutProducer);
           break;
         }
-        // GEMM1 published all 32 slices of the block's rows
+        // GEMM1 published all 32 slices of the block's rows (every lane acquires)
         if (!wait_counter(&a.blk_ready[b], kG1Slices, sAbort, kWaitBudgetNs)) {
           ok = false;
-          fail(kStatusTimeoutProducer);
+          if (lane == 0) fail(kStatusTimeoutProducer);
           break;
         }
-        fence_proxy_async_global();  // generic-proxy stores of other CTAs -> this CTA's TMA reads
         const int4 blk = dbg_block(a.blocks[b], BN, a.e_local, a.pcap, a.status);
-        const int r0 = blk.y;
-        // Only the first R = 2^lg >= nrows rows of each plane tile: the MMA's columns
-        // for rows R..15 read stale shared memory, and their results are never used
-        // (pair rows are stored for t < nrows only).  At decode sizes a block holds a
-        // few rows, so this cuts the CTA's planes load from 64 KB to 4-16 KB.
-        const int lg = blk.z <= 1 ? 0 : blk.z <= 2 ? 1 : blk.z <= 4 ? 2 : blk.z <= 8 ? 3 : 4;
-        const CUtensorMap* tmp = &a.tm_planes[lg];
-        mbar_arrive_expect_tx(planes_full, kIBlocks * 2 * (128u << lg) + 2 * BN * kChunks * 4);
-        for (int kb = 0; kb < kIBlocks; ++kb)
-#pragma unroll
-          for (int pl = 0; pl < 2; ++pl)
-            tma_load_2d(sPlanes + kb * kPlaneKBytes + pl * BN * 128, tmp, planes_full, kb * kBlk, pl * a.pcap + r0,
-                        pol);
-#pragma unroll
-        for (int pl = 0; pl < 2; ++pl)
-          tma_load_2d(sm + kP2PScale + pl * BN * kChunks * 4, &a.tm_pscale, planes_full, r0, pl * kChunks, pol);
+        const int r0 = blk.y, nr = min(blk.z, BN);
+        // planes: [16 K-blocks][2 planes][nr rows][8 chunks of 16 B] into 128B-swizzled tiles
+        const int n_plane_chunks = kIBlocks * 2 * nr * 8;
+        for (int i = lane; i < n_plane_chunks; i += 32) {
+          const int ch = i & 7, rest = i >> 3;
+          const int t = rest % nr, pk = rest / nr;
+          const int kb = pk >> 1, pl = pk & 1;
+          const uint8_t* src = a.planes + ((size_t)pl * a.pcap + r0 + t) * kInter + kb * kBlk + ch * 16;
+          cp_async_16(smem_u32(sPlanes + kb * kPlaneKBytes + pl * BN * 128 + sw128_offset(t, ch)), src, 16u);
+        }
+        // scales: [2 planes][32 chunks][16 rows] fp32, four rows per copy
+        for (int i = lane; i < 2 * kChunks * (BN / 4); i += 32) {
+          const int q4 = i & 3, pc = i >> 2;
+          cp_async_16(smem_u32(sm + kP2PScale + (pc * BN + 4 * q4) * 4), a.plane_scale + (size_t)pc * a.pcap + r0 + 4 * q4,
+                      16u);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        fence_proxy_async_smem();  // generic-proxy shared-memory writes -> the MMA's reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(planes_full);
         ++nblk;
         cur_blk = b;
       }
-      if (nblk > 0 && !mbar_wait_drain(planes_full, (uint32_t)(nblk - 1) & 1u, kWaitBudgetNs))
-        fail(kStatusTimeoutDrain);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -968,8 +971,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&a.tm_w1);
     tma_prefetch_desc(&a.tm_w2);
-    for (int i = 0; i < kPlaneBoxes; ++i) tma_prefetch_desc(&a.tm_planes[i]);
-    tma_prefetch_desc(&a.tm_pscale);
   }
   if (warp == 1) {
     tmem_alloc(sTmem, kTmemCols);
@@ -1022,8 +1023,7 @@ static std::atomic<int> g_decode_mode{0};
 
 int decode_launch_mode() { return g_decode_mode.load(std::memory_order_relaxed); }
 
-cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, const CUtensorMap* tm_planes,
-                          const CUtensorMap* tm_pscale,
+cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2,
                           const uint8_t* hidden, const float* hidden_scale, int T, const float* w1_scale,
                           const float* w2_scale, const Layout& L, uint8_t* ws, void* out, bool f32_out, int num_sms,
                           uint32_t* sink, bool w1_packed, cudaStream_t stream) {
@@ -1032,8 +1032,6 @@ cudaError_t launch_decode(const CUtensorMap* tm_w1, const CUtensorMap* tm_w2, co
   DecodeArgs a;
   a.tm_w1 = *tm_w1;
   a.tm_w2 = *tm_w2;
-  for (int i = 0; i < kPlaneBoxes; ++i) a.tm_planes[i] = tm_planes[i];
-  a.tm_pscale = *tm_pscale;
   a.hidden = hidden;
   a.hidden_scale = hidden_scale;
   a.w1_scale = w1_scale;
