@@ -185,6 +185,11 @@ __device__ __forceinline__ int ld_relaxed_gpu(const int32_t* p) {
   return v;
 }
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void red_release_gpu_add(int32_t* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -493,12 +498,14 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
           for (int j = 0; j < G; ++j) v += sXch[(size_t)(j * 128 + r) * kXchStride + t];
           part[i] = v;
         }
-        __threadfence();
+        // One thread's acq_rel add after the barrier publishes all 512 threads'
+        // partials (release) and, for the last arriver, makes the other segments'
+        // partials visible to all of them after the next barrier (acquire); no
+        // per-thread fence.
         named_barrier_sync(1, kEpi1Threads);
-        if (etid == 0) *sLast = (atomicAdd(&a.split_count[u], 1) == nseg - 1) ? 1 : 0;
+        if (etid == 0) *sLast = (atom_add_acq_rel_gpu(&a.split_count[u], 1) == nseg - 1) ? 1 : 0;
         named_barrier_sync(1, kEpi1Threads);
         last = *sLast != 0;
-        if (last) __threadfence();
       }
       if (last) {
         // SwiGLU: rows 0..63 (first half) pair with rows 64..127 (silu half).  Warp
@@ -578,10 +585,10 @@ __device__ __forceinline__ void gemm1_phase(const DecodeArgs& a, uint8_t* sm, ui
           }
         }
         if (nseg > 1 && etid == 0) a.split_count[u] = 0;  // ready for the next call
-        __threadfence();  // the slice's rows are visible before the block counter moves
       }
       named_barrier_sync(1, kEpi1Threads);
-      // one more of this block's 32 slices is published (GEMM2 waits for all 32)
+      // one more of this block's 32 slices is published (GEMM2 waits for all 32): the
+      // release-add after the barrier covers every thread's plane stores
       if (last && etid == 0) red_release_gpu_add(&a.blk_ready[u / kG1Slices], 1);
     }
   }
