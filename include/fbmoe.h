@@ -160,7 +160,10 @@ FBMOE_API int fbmoe_route(const float* routing_logits, const void* routing_bias,
  * scale = amax / 448 (1 for an all-zero block), q = e4m3(clamp(x / scale, +-448)),
  * round-to-nearest-even -- the reference's 1x128 rule, solution/triton/main.py:
  * 1476-1488 (there applied to its SwiGLU output).  x 16-byte aligned, q 8-byte;
- * values past +-448 saturate to +-448 and NaN stays NaN, as clamp then convert. */
+ * values past +-448 saturate to +-448 and NaN stays NaN, as clamp then convert
+ * (a NaN element converts to an e4m3 NaN of its sign and does not enter its
+ * block's amax; a block holding an infinity gets scale inf).  Results equal the
+ * fp32 division x / scale for every bf16 input. */
 FBMOE_API int fbmoe_quantize_act(const void* x_bf16, int T, void* q_e4m3, float* scale, void* stream);
 
 /* Byte offsets of the forward's intermediate buffers inside the workspace, for
