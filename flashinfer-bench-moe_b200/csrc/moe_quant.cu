@@ -32,7 +32,7 @@
 // this kernel.
 // The path needs amax finite and s >= 2^-64 (so that the residual and the
 // reciprocal stay normal); other blocks (9,183 of the 32,639 finite amax values,
-// all below 1.6e-17, and blocks holding an infinity) divide exactly per element.
+// all below 2.42e-17, and blocks holding an infinity) divide exactly per element.
 // z = +0 for x = -0 (an exact-zero residual drops the sign), so each element's
 // sign bit is carried into its e4m3 byte.  A NaN element converts to an e4m3 NaN
 // that keeps its sign; NaNs do not enter amax (fmaxf).
